@@ -1,0 +1,306 @@
+"""Benchmark: PrunePath MoE-MLP decode latency per layer at batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token (batch 1, tau 0.95) through a stack of ``--layers`` distinct MoE
+layers (default 48; each with its own packed weights in HBM, 3.6 GB in total, so the
+active-expert bytes of one step, ~0.56 GB, are far larger than the 126 MB L2 and no L2
+flush is needed between steps).  The stack is replayed as one CUDA graph of single-launch
+fused-decode kernels chained with programmatic dependent launch: each kernel waits for the
+previous one to finish before it reads its activations, and only prefetches its router
+weights earlier.  Inputs are seeded synthetic layers (4 distinct weight sets, router
+scale 3.5, tau 0.95) and activations ~N(0,1).
+
+value = device time per layer (us) = max over ranks of (CUDA-event time of K graph replays)
+/ (K * layers).  With N > 1 GPUs every rank runs its own replica (decode does not shard):
+weak scaling, the value stays per-layer latency.
+
+Extra keys: roofline of the decode kernel against MEASURED_PEAKS.json (HBM GB/s), e2e
+through TauSparseMoE.forward with pinned host buffers (H2D of x and D2H of the output inside
+the timed region), the CPU oracle baseline, nvidia-smi clocks during the timed region.
+``--impl reference`` times the reference algorithm's CPU path (the oracle restatement of
+MoEBlock/IntegratedOpenPanguMoEMLP, torch CPU bf16, all host threads) on the same metric.
+"""
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "prune_path_openpangu-embedded-1b_b200"
+METRIC = "MoE-MLP decode us/layer @bs1 (% HBM BW); prefill tokens/s @1/2/4/8 GPU"
+H, E, G, TAU = 1536, 64, 96, 0.95
+EXPERT_BYTES = 3 * G * H * 2          # 884,736 B per selected expert
+ROUTER_BYTES = H * E * 2              # 196,608 B
+IO_BYTES = 2 * H * 2                  # x in + out
+
+
+def oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    return importlib.import_module("moe_oracle")
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/ppmoe_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        if not self.proc or not os.path.exists(self.path):
+            return None
+        rows = [r.split(",") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def cpu_baseline(layers, xs, seconds=10.0):
+    """Oracle (reference algorithm, torch CPU bf16) decode bs1 on a bounded sample."""
+    O = oracle()
+    torch.set_num_threads(os.cpu_count() or 1)
+    for i in range(2):
+        O.moe_mlp(xs[i % len(xs)], layers[i % len(layers)], TAU)
+    ts, n, t_end = [], 0, time.perf_counter() + seconds
+    while time.perf_counter() < t_end or n < 5:
+        t0 = time.perf_counter()
+        O.moe_mlp(xs[n % len(xs)], layers[n % len(layers)], TAU)
+        ts.append(time.perf_counter() - t0)
+        n += 1
+    return {"value": statistics.median(ts) * 1e6, "unit": "us/layer", "cores": torch.get_num_threads(),
+            "kind": "port", "sample": f"{n} single-token calls over {len(layers)} layers "
+                                      f"(H={H}, E={E}, G={G}, tau={TAU}), median"}
+
+
+def run_reference(args, rank):
+    """--impl reference: the reference algorithm's own CPU path (oracle restatement)."""
+    if rank != 0:
+        return
+    synth = importlib.import_module(PKG).synth
+    O = oracle()
+    torch.set_num_threads(os.cpu_count() or 1)
+    nl = 4
+    layers = [synth.make_layer(s, H, E, G, router_scale=3.5) for s in range(nl)]
+    xs = [synth.make_tokens(s, 1, H) for s in range(nl)]
+    for w in range(args.warmup):
+        O.moe_mlp(xs[w % nl], layers[w % nl], TAU)
+    t0 = time.perf_counter()
+    for s in range(args.steps):
+        for l in range(nl):
+            O.moe_mlp(xs[(s + l) % nl], layers[l], TAU)
+    dt = time.perf_counter() - t0
+    us = dt / (args.steps * nl) * 1e6
+    line = {"impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "decode bs1, one MoE-MLP layer (config 1)", "hidden": H, "experts": E,
+                       "group": G, "tau": TAU, "layers_per_step": nl},
+            "cpu_baseline": {"value": us, "unit": "us/layer", "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": f"{args.steps} steps x {nl} layers, dense-then-mask oracle"},
+            "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    P = importlib.import_module(PKG)
+    lib = P._lib
+    synth = P.synth
+
+    # ---- layers: 4 distinct weight sets, each mounted on layers/4 modules with own packed blobs
+    nd = 4
+    base = [synth.make_layer(s, H, E, G, router_scale=3.5) for s in range(nd)]
+    mods = []
+    shared = []
+    for s, L in enumerate(base):
+        m0 = P.TauSparseMoE(H, E * G, E, G, TAU).to(dev)
+        P.physical_reorder_for_inference(m0, L.gate_w, L.up_w, L.down_w, L.router_w,
+                                         F.one_hot(L.experts_id, E).t(), TAU)
+        shared.append(m0)
+    for l in range(args.layers):
+        src = shared[l % nd]
+        m = P.TauSparseMoE(H, E * G, E, G, TAU).to(dev)
+        m.W_gate, m.W_up, m.W_down, m.router = src.W_gate, src.W_up, src.W_down, src.router
+        m.packed()  # own blob per layer (distinct HBM)
+        mods.append(m)
+    xs_cpu = [synth.make_tokens(100 + l, 1, H) for l in range(args.layers)]
+    xs = [x.to(dev) for x in xs_cpu]
+    outs = [torch.empty(1, H, dtype=torch.bfloat16, device=dev) for _ in range(args.layers)]
+    ws = mods[0].workspace(1)
+    stream = torch.cuda.Stream(dev)
+    pdl = 0 if args.no_pdl else 1
+
+    # per-layer selected-expert count (for the algorithmic bytes)
+    ks = []
+    for l, m in enumerate(mods):
+        w = torch.empty(1, E, dtype=torch.bfloat16, device=dev)
+        m.forward_decode(xs[l], weights_out=w)
+        ks.append(int((w > 0).sum()))
+    torch.cuda.synchronize()
+    mods[0].check_device_status()
+    step_bytes = sum(k * EXPERT_BYTES + ROUTER_BYTES + IO_BYTES for k in ks)
+
+    def enqueue():
+        h = stream.cuda_stream
+        for l, m in enumerate(mods):
+            lib.call("ppmoe_decode", xs[l].data_ptr(), 1, m._packed.data_ptr(), H, E, G, TAU, None,
+                     outs[l].data_ptr(), None, None, None, ws.data_ptr(), ws.numel(), pdl, h)
+
+    with torch.cuda.stream(stream):
+        enqueue()  # warm the launch configuration cache before capture
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        enqueue()
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    mods[0].check_device_status()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    us_layer = ms * 1e3 / (args.steps * args.layers)
+    launch_us = us_layer  # one kernel per layer
+    achieved = step_bytes / args.layers / (launch_us * 1e-6) / 1e9
+    peak, peak_kind = peaks()
+
+    # ---- e2e: TauSparseMoE.forward with pinned host buffers, copies inside the timed region
+    xh = [x.pin_memory() for x in xs_cpu]
+    oh = [torch.empty(1, H, dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        for l, m in enumerate(mods):
+            xd = xh[l].to(dev, non_blocking=True)
+            y = m(xd.view(1, 1, H))
+            oh[l].copy_(y.view(1, H), non_blocking=True)
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    c1.record()
+    torch.cuda.synchronize()
+    e2e_ms = c0.elapsed_time(c1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_us = e2e_ms * 1e3 / (e2e_steps * args.layers)
+
+    if rank == 0:
+        cpu = cpu_baseline(base, xs_cpu[:8], args.cpu_seconds) if world == 1 else None
+        line = {
+            "metric": METRIC, "value": us_layer, "unit": "us/layer", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) weights x4 distinct sets, N(0,1) activations)",
+            "config": {"workload": "decode bs1, one MoE-MLP layer (config 1)", "hidden": H, "experts": E,
+                       "group": G, "tau": TAU, "router_scale": 3.5, "layers_per_step": args.layers,
+                       "mean_active_experts": sum(ks) / len(ks), "pdl": bool(pdl),
+                       "l2": "no flush: each step streams ~%.0f MB of distinct active weights (> 126 MB L2)"
+                             % (step_bytes / 1e6),
+                       "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": None, "bytes_per_launch": step_bytes / args.layers,
+                         "kernel": "decode_fused_kernel<1,1>"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": args.layers * H * 2,
+                    "d2h_bytes_per_step": args.layers * H * 2,
+                    "path": "TauSparseMoE.forward, eager, pinned host x/out"},
+            "gpu_launches": args.steps * args.layers,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,111 @@
+/*
+ * ppmoe.h -- C ABI of the B200 (sm_100a) PrunePath sparse-MoE MLP library (libppmoe.so).
+ *
+ * Plain pointers and sizes only.  Every tensor pointer is DEVICE memory owned by the caller
+ * unless stated otherwise; bf16 tensors are passed as `void*` (2-byte IEEE bfloat16,
+ * row-major, contiguous).  `stream` is a `cudaStream_t` passed as `void*` (NULL = legacy
+ * default stream).  Every call returns an int status: 0 = ok, negative = error (see
+ * PPMOE_ERR_*); `ppmoe_last_error()` gives the message of the last failing call on the
+ * calling host thread.  Launches are asynchronous; device-side faults that the kernels
+ * detect (a bounded wait that ran out) are recorded in the workspace and returned by
+ * `ppmoe_workspace_status()`.
+ *
+ * Shapes: hidden H, experts E, neurons per expert G, intermediate I = E * G.
+ * Supported: H % 64 == 0, H <= 4096, 1 <= E <= 256, G % 8 == 0, G <= 256.
+ *
+ * The reference exposes this path only as the PyTorch module `TauSparseMoE`
+ * (src/tl_kernel_optimized_Ultimate_PanGU.py:468-615); each entry point below names the
+ * part of that module (or of its callers) it replaces.
+ */
+#ifndef PPMOE_H_
+#define PPMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PPMOE_API __attribute__((visibility("default")))
+#else
+#define PPMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PPMOE_OK 0
+#define PPMOE_ERR_INVALID_ARG (-1)  /* null pointer, bad size or misaligned buffer */
+#define PPMOE_ERR_UNSUPPORTED (-2)  /* shape outside the supported range */
+#define PPMOE_ERR_TIMEOUT (-3)      /* a bounded device-side wait ran out (status word) */
+#define PPMOE_ERR_CUDA (-4)         /* a CUDA runtime call failed */
+#define PPMOE_ERR_WORKSPACE (-5)    /* workspace too small or not initialised */
+
+/* Largest token count the fused decode kernel takes; larger batches use the prefill path
+ * (the reference takes its decode path only at one token, tl:612-615). */
+#define PPMOE_DECODE_MAX_TOKENS 16
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+PPMOE_API int ppmoe_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+PPMOE_API const char* ppmoe_last_error(void);
+
+/* ---------------------------------------------------------------------------------------
+ * Packed weights.  Replaces the layout that `physical_reorder_for_inference`
+ * (src/openpangu_moe.py:212-256) mounts on TauSparseMoE's buffers W_gate [H,I],
+ * W_up [H,I], W_down [I,H], router [H,E] (tl:483-486): this call reads exactly those
+ * buffers and writes one packed, 1 KiB-aligned blob:
+ *   router_he [H][E] | router_eh [E][H] | experts [E][G][3][H] (gate row, up row, down row
+ *   of each neuron, contiguous) | down_t [E][H][G]
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API size_t ppmoe_packed_bytes(int hidden, int experts, int group);
+PPMOE_API int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_down, const void* router,
+               int hidden, int experts, int group, void* packed, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Workspace: scratch the kernels keep between calls (cross-cluster partial sums,
+ * self-resetting arrival counters, the device status word).  Size it with
+ * ppmoe_workspace_bytes for the largest token count the caller will pass and zero it once
+ * with ppmoe_workspace_init.  One workspace must not be used by two calls that can run
+ * concurrently (different streams).
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API size_t ppmoe_workspace_bytes(int max_tokens, int hidden, int experts, int group);
+PPMOE_API int ppmoe_workspace_init(void* ws, size_t ws_bytes, void* stream);
+/* Synchronises `stream`, returns PPMOE_OK or the first device-side error recorded since the
+ * last call, and clears it. */
+PPMOE_API int ppmoe_workspace_status(void* ws, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Router selection from given bf16 logits [N][E] (softmax, descending-probability order with
+ * ties to the lower expert index, bf16 cumulative mass < bf16(tau), forced top-1).
+ * Replaces `softmax_thresholding` (src/MoEBlock.py:49-95) and the selection half of
+ * moe_router_select_kernel_decode (tl:356-380) / moe_select_expert_kernel (tl:96-124).
+ * weights_out [N][E] bf16: sigmoid(logit) on selected experts, 0 elsewhere (required).
+ * mask_out [N][E] uint8 (optional, may be NULL).
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API int ppmoe_route_logits(const void* logits, int tokens, int experts, float tau,
+                       void* weights_out, uint8_t* mask_out, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Fused decode, 1 <= tokens <= PPMOE_DECODE_MAX_TOKENS: router GEMV + selection + expert
+ * SwiGLU + down projection in ONE launch.  Replaces TauSparseMoE.forward_decode
+ * (tl:494-530: moe_router_select_kernel_decode + moe_decode_swiglu_fused_kernel).
+ *   x [N][H] bf16 -> out [N][H] bf16.
+ *   logit_bias: optional fp32 [E] added to the bf16 logits (then rounded to bf16) before
+ *     selection; NULL for the reference's bias-free router.
+ *   logits_out [N][E] bf16, weights_out [N][E] bf16, counts [E] int64 (+= number of tokens
+ *     that selected each expert, the reference's activated_statistics,
+ *     src/MoEBlock.py:189-191): optional, NULL to skip.
+ *   pdl != 0 launches with programmatic dependent launch: the kernel prefetches its router
+ *     slice before waiting on the previous kernel in the stream.
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int experts,
+                 int group, float tau, const float* logit_bias, void* out, void* logits_out,
+                 void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
+                 void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PPMOE_H_ */

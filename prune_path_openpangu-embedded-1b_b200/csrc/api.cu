@@ -1,0 +1,164 @@
+// extern "C" entry points of libppmoe (declared in include/ppmoe.h): argument validation,
+// workspace layout, error reporting.  The kernels live in pack.cu, route.cu, decode.cu.
+#include <stdarg.h>
+#include <string.h>
+#include "common.cuh"
+
+namespace ppmoe {
+
+static thread_local char g_err[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  set_error("%s failed: %s", what, cudaGetErrorString(e));
+  return PPMOE_ERR_CUDA;
+}
+
+int pack_launch(const void*, const void*, const void*, const void*, int, int, int, void*, cudaStream_t);
+int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t);
+int decode_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*,
+                  int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
+
+// Workspace header: status word, decode arrival counters; then the decode cluster partials.
+constexpr size_t kWsHeader = 256;
+constexpr size_t kWsCounters = 64;
+constexpr int kWsMaxClusters = 32;
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int check_shape(const char* fn, int H, int E, int G) {
+  if (H <= 0 || H % 64 != 0 || H > 4096) {
+    set_error("%s: hidden=%d must be a positive multiple of 64 <= 4096", fn, H);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (E <= 0 || E > 256) {
+    set_error("%s: experts=%d must be in [1, 256]", fn, E);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (G <= 0 || G % 8 != 0 || G > 256) {
+    set_error("%s: group=%d must be a positive multiple of 8 <= 256", fn, G);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  return PPMOE_OK;
+}
+
+}  // namespace ppmoe
+
+using namespace ppmoe;
+
+extern "C" {
+
+int ppmoe_version(void) { return 100; }
+
+const char* ppmoe_last_error(void) { return g_err; }
+
+size_t ppmoe_packed_bytes(int hidden, int experts, int group) {
+  if (check_shape("ppmoe_packed_bytes", hidden, experts, group)) return 0;
+  return packed_layout(hidden, experts, group).total;
+}
+
+int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_down, const void* router, int hidden,
+               int experts, int group, void* packed, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_shape("ppmoe_pack", hidden, experts, group)) return rc;
+  if (!W_gate || !W_up || !W_down || !router || !packed) {
+    set_error("ppmoe_pack: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (!aligned(packed, 1024)) {
+    set_error("ppmoe_pack: packed buffer must be 1024-byte aligned");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return pack_launch(W_gate, W_up, W_down, router, hidden, experts, group, packed,
+                     static_cast<cudaStream_t>(stream));
+}
+
+size_t ppmoe_workspace_bytes(int max_tokens, int hidden, int experts, int group) {
+  if (check_shape("ppmoe_workspace_bytes", hidden, experts, group) || max_tokens < 0) return 0;
+  const size_t nt = (size_t)(max_tokens < PPMOE_DECODE_MAX_TOKENS ? max_tokens : PPMOE_DECODE_MAX_TOKENS);
+  return kWsHeader + (size_t)kWsMaxClusters * (nt ? nt : 1) * hidden * 4;
+}
+
+int ppmoe_workspace_init(void* ws, size_t ws_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!ws || ws_bytes < kWsHeader || !aligned(ws, 256)) {
+    set_error("ppmoe_workspace_init: workspace must be >= %zu bytes and 256-byte aligned", kWsHeader);
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, kWsHeader, static_cast<cudaStream_t>(stream)));
+  return PPMOE_OK;
+}
+
+int ppmoe_workspace_status(void* ws, void* stream) {
+  g_err[0] = 0;
+  if (!ws) {
+    set_error("ppmoe_workspace_status: null workspace");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t word = 0;
+  PPMOE_CHECK_CUDA(cudaMemcpyAsync(&word, ws, 4, cudaMemcpyDeviceToHost, st));
+  PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
+  if (word == 0) return PPMOE_OK;
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 4, st));
+  // a timed-out launch may have left arrival counters armed: re-arm them too
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(ws) + kWsCounters, 0, 64, st));
+  PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
+  if (word & DEVERR_TIMEOUT) {
+    set_error("device: a bounded wait timed out (status 0x%x)", word);
+    return PPMOE_ERR_TIMEOUT;
+  }
+  set_error("device: capacity exceeded (status 0x%x)", word);
+  return PPMOE_ERR_WORKSPACE;
+}
+
+int ppmoe_route_logits(const void* logits, int tokens, int experts, float tau, void* weights_out,
+                       uint8_t* mask_out, void* stream) {
+  g_err[0] = 0;
+  if (tokens < 0 || experts <= 0 || experts > 256) {
+    set_error("ppmoe_route_logits: tokens=%d experts=%d out of range", tokens, experts);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (tokens > 0 && (!logits || !weights_out)) {
+    set_error("ppmoe_route_logits: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return route_logits_launch(logits, tokens, experts, tau, nullptr, weights_out, mask_out,
+                             static_cast<cudaStream_t>(stream));
+}
+
+int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
+                 const float* logit_bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
+                 void* ws, size_t ws_bytes, int pdl, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_shape("ppmoe_decode", hidden, experts, group)) return rc;
+  if (tokens < 1 || tokens > PPMOE_DECODE_MAX_TOKENS) {
+    set_error("ppmoe_decode: tokens=%d must be in [1, %d]", tokens, PPMOE_DECODE_MAX_TOKENS);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (!x || !packed || !out || !ws) {
+    set_error("ppmoe_decode: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(packed, 1024) || !aligned(ws, 256)) {
+    set_error("ppmoe_decode: x/out must be 16-byte, packed 1024-byte, ws 256-byte aligned");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (ws_bytes < kWsHeader) {
+    set_error("ppmoe_decode: workspace too small");
+    return PPMOE_ERR_WORKSPACE;
+  }
+  uint8_t* w8 = static_cast<uint8_t*>(ws);
+  return decode_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, out, logits_out, weights_out,
+                       counts, ws, ws_bytes, pdl, static_cast<cudaStream_t>(stream),
+                       reinterpret_cast<uint32_t*>(w8), reinterpret_cast<uint32_t*>(w8 + kWsCounters),
+                       reinterpret_cast<float*>(w8 + kWsHeader), ws_bytes - kWsHeader);
+}
+
+}  // extern "C"

@@ -1,0 +1,494 @@
+// Fused decode: router GEMV + tau selection + expert SwiGLU + down projection, ONE launch.
+//
+// Replaces TauSparseMoE.forward_decode (src/tl_kernel_optimized_Ultimate_PanGU.py:494-530),
+// i.e. moe_router_select_kernel_decode (tl:335-380) followed by
+// moe_decode_swiglu_fused_kernel (tl:385-462), for 1..16 tokens.
+//
+// Grid: C clusters x 8 CTAs (C = the number of 8-CTA clusters the GPU co-schedules), 384
+// threads per CTA, one CTA per SM.
+//
+//  1. Router.  Rank r of every cluster loads rows [r*H/8, (r+1)*H/8) of router_he
+//     ([H][E], contiguous) with one bulk copy, computes partial logits for all tokens in a
+//     fixed order, and the 8 partials are combined over distributed shared memory in rank
+//     order.  Every cluster computes the same logits with the same operation order, so every
+//     CTA holds bit-identical selections without any grid-wide barrier.
+//  2. Selection (select.cuh), redundantly in every CTA: gate weights, union of selected
+//     experts, per-expert token bitmask.
+//  3. Experts.  The union's neurons (|U| * G) are split evenly over all CTAs of the grid.
+//     Each neuron is one contiguous 3*H*2-byte record (gate row | up row | down row) that
+//     a bulk copy streams into a ring of shared-memory slots; 12 warps each compute one
+//     neuron's gate/up dot products for the tokens that selected its expert
+//     (g,u -> bf16; s=bf16(silu(g)); a=bf16(s*u); a2=bf16(a*w)), then all threads apply the
+//     12 down rows to their fp32 output accumulators (4 hidden columns x tokens each).
+//  4. Reduction.  The 8 CTA partials of a cluster are summed over distributed shared
+//     memory (rank order) into one partial per cluster in global scratch; per 1/8-slice of
+//     the hidden dimension an arrival counter elects the last cluster, whose CTA sums the
+//     C cluster partials in cluster order and writes bf16 output, then re-arms the counter.
+//     The result is deterministic (fixed summation order) and rounded to bf16 exactly once.
+//
+// No CTA ever waits for another cluster, so co-residency of the grid is not required.
+// Every mbarrier wait is bounded (common.cuh) and records a status bit instead of hanging.
+#include <cooperative_groups.h>
+#include "common.cuh"
+#include "select.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace ppmoe {
+
+constexpr int kDecThreads = 384;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kCluster = 8;
+constexpr int kMaxClusters = 32;  // workspace sizing (148 SMs -> at most 18 clusters of 8)
+
+struct DecodeArgs {
+  const __nv_bfloat16* x;
+  int N;
+  const __nv_bfloat16* router_he;  // [H][E]
+  const __nv_bfloat16* experts;    // [E][G][3][H]
+  int H, E, G;
+  float tau_b;
+  const float* bias;
+  __nv_bfloat16* out;
+  __nv_bfloat16* logits_out;
+  __nv_bfloat16* weights_out;
+  long long* counts;
+  float* cpart;        // [clusters][N][H]
+  uint32_t* counters;  // [8]
+  uint32_t* status;
+  int slots;           // ring depth
+  int pdl;
+};
+
+// Shared-memory carve-out (byte offsets from a 1 KiB aligned base).
+struct DecSmem {
+  uint32_t bars, x, part, lg, w, tokmask, ulist, misc, a2, ring, total;
+};
+
+__host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
+  DecSmem s;
+  uint32_t o = 0;
+  s.bars = o;    o += 8 * 64;                                   // <= 63 slot barriers + 1
+  s.x = o;       o = (uint32_t)align_up(o + (size_t)NT * H * 2, 128);
+  s.part = o;    o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
+  s.lg = o;      o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
+  s.w = o;       o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
+  s.tokmask = o; o = (uint32_t)align_up(o + (size_t)E * 4, 128);
+  s.ulist = o;   o = (uint32_t)align_up(o + (size_t)E * 4, 128);
+  s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
+  s.a2 = o;      o = (uint32_t)align_up(o + (size_t)kDecWarps * NT * 4, 1024);
+  s.ring = o;    o += (uint32_t)slots * 3u * (uint32_t)H * 2u;
+  s.total = o;
+  return s;
+}
+
+template <int NT, int HCH>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rank = (int)cluster.block_rank();
+  const int cid = blockIdx.x / kCluster;
+  const int nclusters = gridDim.x / kCluster;
+  const int H = a.H, E = a.E, G = a.G, N = a.N;
+  const int HS = H / kCluster;  // router rows / output columns owned by this rank
+  const DecSmem L = dec_smem(NT, H, E, a.slots);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* bar_in = bars + a.slots;  // x + router slice
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + L.x);
+  float* part = reinterpret_cast<float*>(smem + L.part);
+  float* lg = reinterpret_cast<float*>(smem + L.lg);
+  float* ws = reinterpret_cast<float*>(smem + L.w);
+  uint32_t* tokmask = reinterpret_cast<uint32_t*>(smem + L.tokmask);
+  int* ulist = reinterpret_cast<int*>(smem + L.ulist);
+  int* misc = reinterpret_cast<int*>(smem + L.misc);  // [0]=|U| [1]=is_last
+  float* a2s = reinterpret_cast<float*>(smem + L.a2);
+  uint8_t* ring = smem + L.ring;
+  const uint32_t rec_bytes = 3u * (uint32_t)H * 2u;
+
+  // ---- prologue: barriers; router slice prefetch (weights only: legal before the PDL wait)
+  if (tid == 0) {
+    for (int s = 0; s <= a.slots; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t rs_bytes = (uint32_t)HS * (uint32_t)E * 2u;
+  const uint32_t x_bytes = (uint32_t)N * (uint32_t)H * 2u;
+  __nv_bfloat16* rs = reinterpret_cast<__nv_bfloat16*>(ring);  // router slice aliases the ring
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_in, rs_bytes + x_bytes);
+    bulk_g2s(rs, a.router_he + (size_t)rank * HS * E, rs_bytes, bar_in, policy_evict_last());
+  }
+  if (a.pdl) pdl_wait();
+  if (tid == 0) bulk_g2s(xs, a.x, x_bytes, bar_in, policy_evict_first());
+  // zero-fill padded token rows so the router partials stay finite
+  for (int i = N * H + tid; i < NT * H; i += kDecThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = tid; i < E; i += kDecThreads) tokmask[i] = 0u;
+  mbar_wait(bar_in, 0, a.status);
+
+  // ---- 1. router partial over this rank's K-slice: thread (group g, expert e)
+  {
+    const int KG = max(1, kDecThreads / E);
+    const int g = tid / E, e = tid - g * E;
+    float acc[NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
+    if (g < KG) {
+      for (int k = g; k < HS; k += KG) {
+        const float r = __bfloat162float(rs[(size_t)k * E + e]);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = fmaf(__bfloat162float(xs[t * H + rank * HS + k]), r, acc[t]);
+      }
+    }
+    // fixed-order combine of the KG groups through the (still free) ring tail
+    float* scratch = reinterpret_cast<float*>(ring + align_up(rs_bytes, 128));
+    if (g < KG) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t) scratch[(g * NT + t) * E + e] = acc[t];
+    }
+    __syncthreads();
+    for (int i = tid; i < NT * E; i += kDecThreads) {
+      float s = 0.f;
+      for (int q = 0; q < KG; ++q) s += scratch[q * NT * E + i];
+      part[i] = s;
+    }
+  }
+  cluster.sync();  // partials visible cluster-wide
+
+  // ---- full logits: sum the 8 rank partials in rank order
+  for (int i = tid; i < N * E; i += kDecThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) s += cluster.map_shared_rank(part, q)[i];
+    float l = bf16r(s);
+    if (a.bias) l = bf16r(l + a.bias[i % E]);
+    lg[i] = l;
+  }
+  __syncthreads();
+
+  // ---- 2. selection, one warp per token
+  for (int t = warp; t < N; t += kDecWarps) {
+    float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+      const int e = lane + 32 * i;
+      l[i] = e < E ? lg[t * E + e] : -INFINITY;
+    }
+    const uint32_t bits = select_experts_warp(l, E, a.tau_b, w);
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) {
+        ws[t * E + e] = w[i];
+        if ((bits >> i) & 1u) atomicOr(&tokmask[e], 1u << t);
+      }
+    }
+  }
+  __syncthreads();
+  // union list in ascending expert order (warp 0, ballot compaction)
+  if (warp == 0) {
+    int base = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const bool on = e < E && tokmask[e] != 0u;
+      const uint32_t b = __ballot_sync(0xffffffffu, on);
+      if (on) ulist[base + __popc(b & ((1u << lane) - 1u))] = e;
+      base += __popc(b);
+    }
+    if (lane == 0) misc[0] = base;
+  }
+  // optional side outputs from the first CTA of the grid
+  if (blockIdx.x == 0) {
+    for (int i = tid; i < N * E; i += kDecThreads) {
+      if (a.logits_out) a.logits_out[i] = __float2bfloat16_rn(lg[i]);
+      if (a.weights_out) a.weights_out[i] = __float2bfloat16_rn(ws[i]);
+    }
+    if (a.counts) {
+      for (int e = tid; e < E; e += kDecThreads) {
+        long long c = 0;
+        for (int t = 0; t < N; ++t) c += ws[t * E + e] > 0.f;
+        a.counts[e] += c;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- 3. experts: this CTA's neuron range of the union
+  const int nU = misc[0];
+  const long long W = (long long)nU * G;
+  const long long i0 = W * blockIdx.x / gridDim.x, i1 = W * (blockIdx.x + 1) / gridDim.x;
+  const int cnt = (int)(i1 - i0);
+  const uint64_t pol = policy_evict_first();
+  auto issue = [&](int n) {  // neuron n of this CTA -> slot n % slots
+    const long long gi = i0 + n;
+    const int e = ulist[gi / G], j = (int)(gi % G);
+    const int s = n % a.slots;
+    mbar_arrive_expect_tx(&bars[s], rec_bytes);
+    bulk_g2s(ring + (size_t)s * rec_bytes, a.experts + ((size_t)e * G + j) * 3 * H, rec_bytes, &bars[s], pol);
+  };
+  // the router slice / scratch in the ring must be dead before the first record lands
+  __syncthreads();
+  if (tid == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (int n = 0; n < min(cnt, a.slots); ++n) issue(n);
+  }
+
+  float acc[HCH][NT][4];
+#pragma unroll
+  for (int c = 0; c < HCH; ++c)
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[c][t][q] = 0.f;
+
+  for (int b0 = 0; b0 < cnt; b0 += kDecWarps) {
+    const int n = b0 + warp;
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+      if (lane == t) a2s[warp * NT + t] = 0.f;
+    __syncwarp();
+    if (n < cnt) {
+      const int s = n % a.slots;
+      mbar_wait(&bars[s], (uint32_t)((n / a.slots) & 1), a.status);
+      const long long gi = i0 + n;
+      const int u = (int)(gi / G);
+      const int e = ulist[u];
+      uint32_t tm = tokmask[e];
+      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes);
+      const __nv_bfloat16* up = gate + H;
+      while (tm) {
+        const int t = __ffs(tm) - 1;
+        tm &= tm - 1u;
+        float sg = 0.f, su = 0.f;
+        for (int v = lane; v < H / 8; v += 32) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + v * 8);
+          const uint4 gv = *reinterpret_cast<const uint4*>(gate + v * 8);
+          const uint4 uv = *reinterpret_cast<const uint4*>(up + v * 8);
+          const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
+          const __nv_bfloat162* gp = reinterpret_cast<const __nv_bfloat162*>(&gv);
+          const __nv_bfloat162* up2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 xf = __bfloat1622float2(xp[q]);
+            const float2 gf = __bfloat1622float2(gp[q]);
+            const float2 uf = __bfloat1622float2(up2[q]);
+            sg = fmaf(xf.x, gf.x, sg); sg = fmaf(xf.y, gf.y, sg);
+            su = fmaf(xf.x, uf.x, su); su = fmaf(xf.y, uf.y, su);
+          }
+        }
+        sg = warp_sum(sg);
+        su = warp_sum(su);
+        if (lane == 0) {
+          const float gb = bf16r(sg), ub = bf16r(su);
+          const float sb = bf16r(__fdiv_rn(gb, 1.f + expf(-gb)));
+          const float ab = bf16r(sb * ub);
+          a2s[warp * NT + t] = bf16r(ab * ws[t * E + e]);
+        }
+      }
+    }
+    __syncthreads();
+    // down rows of this batch into the fp32 accumulators
+    const int nb = min(kDecWarps, cnt - b0);
+    for (int m = 0; m < nb; ++m) {
+      const int s = (b0 + m) % a.slots;
+      const __nv_bfloat16* down = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes) + 2 * H;
+      float av[NT];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) av[t] = a2s[m * NT + t];
+#pragma unroll
+      for (int c = 0; c < HCH; ++c) {
+        const int h4 = tid + c * kDecThreads;
+        if (h4 < H / 4) {
+          const uint2 dv = *reinterpret_cast<const uint2*>(down + h4 * 4);
+          const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.x));
+          const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.y));
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            acc[c][t][0] = fmaf(av[t], d01.x, acc[c][t][0]);
+            acc[c][t][1] = fmaf(av[t], d01.y, acc[c][t][1]);
+            acc[c][t][2] = fmaf(av[t], d23.x, acc[c][t][2]);
+            acc[c][t][3] = fmaf(av[t], d23.y, acc[c][t][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int m = 0; m < nb; ++m)
+        if (b0 + m + a.slots < cnt) issue(b0 + m + a.slots);
+    }
+  }
+  if (a.pdl) pdl_launch_dependents();
+
+  // ---- 4a. CTA partial -> shared (ring is idle: every issued record has been consumed)
+  float* red = reinterpret_cast<float*>(ring);
+#pragma unroll
+  for (int c = 0; c < HCH; ++c) {
+    const int h4 = tid + c * kDecThreads;
+    if (h4 < H / 4) {
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (t < N)
+          *reinterpret_cast<float4*>(red + (size_t)t * H + h4 * 4) =
+              make_float4(acc[c][t][0], acc[c][t][1], acc[c][t][2], acc[c][t][3]);
+    }
+  }
+  cluster.sync();
+  // ---- 4b. cluster partial of this rank's column slice, rank order
+  for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
+    const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q) {
+      const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, q) + (size_t)t * H + h);
+      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    *reinterpret_cast<float4*>(a.cpart + ((size_t)cid * N + t) * H + h) = s;
+  }
+  cluster.sync();  // peers finished reading this CTA's shared memory
+  // ---- 4c. last cluster to finish this slice sums all cluster partials
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t old = atomicAdd(&a.counters[rank], 1u);
+    misc[1] = (old == (uint32_t)nclusters - 1u);
+  }
+  __syncthreads();
+  if (misc[1]) {
+    __threadfence();
+    for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
+      const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
+      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < nclusters; ++c) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.cpart + ((size_t)c * N + t) * H + h));
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      }
+      __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(a.out + (size_t)t * H + h) = pk;
+    }
+    if (tid == 0) a.counters[rank] = 0u;  // re-arm for the next launch
+  }
+}
+
+// ------------------------------------------------------------------ host side
+using KernelFn = void (*)(const DecodeArgs);
+
+static KernelFn pick_kernel(int NT, int HCH) {
+#define PPMOE_K(nt, hch) if (NT == nt && HCH == hch) return decode_fused_kernel<nt, hch>;
+  PPMOE_K(1, 1) PPMOE_K(1, 2) PPMOE_K(1, 3)
+  PPMOE_K(2, 1) PPMOE_K(2, 2) PPMOE_K(2, 3)
+  PPMOE_K(4, 1) PPMOE_K(4, 2) PPMOE_K(4, 3)
+  PPMOE_K(8, 1) PPMOE_K(8, 2)
+  PPMOE_K(16, 1)
+#undef PPMOE_K
+  return nullptr;
+}
+
+struct DecodeCfgCache {
+  int dev = -1, NT = 0, H = 0, E = 0, slots = 0, pdl = -1;
+  uint32_t smem = 0;
+  int clusters = 0;
+};
+static thread_local DecodeCfgCache g_dec_cache;
+
+int decode_launch(const void* x, int tokens, const void* packed, int H, int E, int G, float tau,
+                  const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
+                  void* wsp, size_t ws_bytes, int pdl, cudaStream_t stream, uint32_t* status,
+                  uint32_t* counters, float* cpart, size_t cpart_bytes) {
+  int NT = 1;
+  while (NT < tokens) NT <<= 1;
+  const int HCH = (H / 4 + kDecThreads - 1) / kDecThreads;
+  KernelFn fn = pick_kernel(NT, HCH);
+  if (!fn) {
+    set_error("ppmoe_decode: tokens=%d with hidden=%d is outside the decode kernel's range", tokens, H);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  int dev = 0;
+  PPMOE_CHECK_CUDA(cudaGetDevice(&dev));
+  DecodeCfgCache& C = g_dec_cache;
+  if (C.dev != dev || C.NT != NT || C.H != H || C.E != E || C.pdl != pdl) {
+    int max_optin = 0;
+    PPMOE_CHECK_CUDA(cudaDeviceGetAttribute(&max_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    int slots = 24;
+    DecSmem L = dec_smem(NT, H, E, slots);
+    while (slots > 2 && L.total + 1024 > (uint32_t)max_optin) L = dec_smem(NT, H, E, --slots);
+    // the router slice and its group scratch alias the ring
+    const size_t need_ring = align_up((size_t)(H / kCluster) * E * 2, 128) +
+                             (size_t)max(1, kDecThreads / E) * NT * E * 4;
+    const size_t red_ring = (size_t)NT * H * 4;
+    if ((size_t)slots * 3 * H * 2 < need_ring || (size_t)slots * 3 * H * 2 < red_ring ||
+        L.total + 1024 > (uint32_t)max_optin || slots < 2) {
+      set_error("ppmoe_decode: shared memory budget exceeded (H=%d E=%d tokens=%d)", H, E, tokens);
+      return PPMOE_ERR_UNSUPPORTED;
+    }
+    const uint32_t smem = L.total + 1024;
+    PPMOE_CHECK_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    int nsm = 0;
+    PPMOE_CHECK_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    cfg.gridDim = dim3((nsm / kCluster) * kCluster);
+    cfg.blockDim = dim3(kDecThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    PPMOE_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg));
+    if (clusters <= 0) {
+      set_error("ppmoe_decode: no 8-CTA cluster fits (smem=%u)", smem);
+      return PPMOE_ERR_UNSUPPORTED;
+    }
+    C.dev = dev; C.NT = NT; C.H = H; C.E = E; C.slots = slots; C.pdl = pdl;
+    C.smem = smem; C.clusters = min(clusters, kMaxClusters);
+  }
+  if ((size_t)C.clusters * tokens * H * 4 > cpart_bytes) {
+    set_error("ppmoe_decode: workspace sized for fewer tokens than %d", tokens);
+    return PPMOE_ERR_WORKSPACE;
+  }
+  const PackedLayout PL = packed_layout(H, E, G);
+  DecodeArgs a;
+  a.x = static_cast<const __nv_bfloat16*>(x);
+  a.N = tokens;
+  a.router_he = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.router_he);
+  a.experts = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.experts);
+  a.H = H; a.E = E; a.G = G;
+  a.tau_b = __bfloat162float(__float2bfloat16_rn(tau));
+  a.bias = bias;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.logits_out = static_cast<__nv_bfloat16*>(logits_out);
+  a.weights_out = static_cast<__nv_bfloat16*>(weights_out);
+  a.counts = reinterpret_cast<long long*>(counts);
+  a.cpart = cpart;
+  a.counters = counters;
+  a.status = status;
+  a.slots = C.slots;
+  a.pdl = pdl;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(C.clusters * kCluster);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = C.smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  PPMOE_CHECK_CUDA(cudaLaunchKernelEx(&cfg, fn, a));
+  return PPMOE_OK;
+}
+
+}  // namespace ppmoe

@@ -1,0 +1,48 @@
+// Selection from given logits: softmax_thresholding (src/MoEBlock.py:49-95) on the GPU,
+// one warp per token (select.cuh).  Used by the prefill path after its router GEMM and
+// exported on its own so the selection contract can be checked from fixed bf16 logits.
+#include "common.cuh"
+#include "select.cuh"
+
+namespace ppmoe {
+
+__global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, int N, int E, float tau_b,
+                                    const float* __restrict__ bias, __nv_bfloat16* __restrict__ w_out,
+                                    uint8_t* __restrict__ mask_out) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= N) return;
+  float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    float v = -INFINITY;
+    if (e < E) {
+      v = __bfloat162float(logits[(size_t)t * E + e]);
+      if (bias) v = bf16r(v + bias[e]);
+    }
+    l[i] = v;
+  }
+  const uint32_t bits = select_experts_warp(l, E, tau_b, w);
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      w_out[(size_t)t * E + e] = __float2bfloat16_rn(w[i]);
+      if (mask_out) mask_out[(size_t)t * E + e] = (bits >> i) & 1u;
+    }
+  }
+}
+
+int route_logits_launch(const void* logits, int N, int E, float tau, const float* bias, void* w_out,
+                        uint8_t* mask_out, cudaStream_t st) {
+  if (N == 0) return PPMOE_OK;
+  const int warps = 8;
+  route_logits_kernel<<<(N + warps - 1) / warps, warps * 32, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(logits), N, E, __bfloat162float(__float2bfloat16_rn(tau)), bias,
+      static_cast<__nv_bfloat16*>(w_out), mask_out);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return PPMOE_OK;
+}
+
+}  // namespace ppmoe

@@ -1,0 +1,182 @@
+"""Drop-in ``TauSparseMoE`` backed by the sm_100a kernels of libppmoe.
+
+Mirrors the reference module ``TauSparseMoE``
+(src/tl_kernel_optimized_Ultimate_PanGU.py:468-615):
+
+* constructor ``TauSparseMoE(hidden_size, intermediate_size, num_experts, group_size, tau)``;
+* persistent bf16 buffers ``W_gate [H,I]``, ``W_up [H,I]``, ``W_down [I,H]``,
+  ``router [H,E]`` (tl:483-486) -- the state-dict keys ``...mlp.tau_moe.{W_gate,W_up,W_down,
+  router}`` and the tensors ``physical_reorder_for_inference`` assigns through ``.data``
+  (src/openpangu_moe.py:239-243);
+* mutable attribute ``tau`` (src/openpangu_moe.py:226);
+* ``forward(x [B,L,H]) -> [B,L,H]`` bf16 (tl:606-615): up to 16 tokens go through the
+  fused single-launch decode kernel, more tokens through the prefill path.
+
+The packed layout the kernels read is derived on the device from those four buffers and
+rebuilt automatically whenever one of them is replaced or modified in place.  Every call is
+enqueued on the current CUDA stream without host synchronisation.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+__all__ = ["TauSparseMoE", "IntegratedOpenPanguMoEMLP", "physical_reorder_for_inference"]
+
+
+def _stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class TauSparseMoE(nn.Module):
+    """B200 tau-sparse MoE MLP with the reference module's interface."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, num_experts: int,
+                 group_size: int, tau: float):
+        super().__init__()
+        if intermediate_size != num_experts * group_size:
+            raise ValueError("intermediate_size must equal num_experts * group_size")
+        self.hidden_size = hidden_size
+        self.intermediate_size = intermediate_size
+        self.num_experts = num_experts
+        self.group_size = group_size
+        self.tau = tau
+        self.logit_bias = None  # optional fp32 [E] prior (skewed-routing benchmarks)
+        self.track_statistics = False
+        self.register_buffer("W_gate", torch.empty(hidden_size, intermediate_size, dtype=torch.bfloat16))
+        self.register_buffer("W_up", torch.empty(hidden_size, intermediate_size, dtype=torch.bfloat16))
+        self.register_buffer("W_down", torch.empty(intermediate_size, hidden_size, dtype=torch.bfloat16))
+        self.register_buffer("router", torch.empty(hidden_size, num_experts, dtype=torch.bfloat16))
+        # per-expert count of tokens with a positive gate weight (src/MoEBlock.py:146,189-191)
+        self.register_buffer("activated_statistics", torch.zeros(num_experts, dtype=torch.long),
+                             persistent=False)
+        self._packed = None
+        self._packed_key = None
+        self._ws = None
+        self._ws_tokens = 0
+        self._prefill = None
+
+    # ------------------------------------------------------------------ packing
+    def _weights_key(self):
+        return tuple((t.data_ptr(), t._version, t.device) for t in
+                     (self.W_gate, self.W_up, self.W_down, self.router))
+
+    def packed(self) -> torch.Tensor:
+        """The packed weight blob (uint8, 1 KiB aligned), rebuilt if any buffer changed."""
+        key = self._weights_key()
+        if self._packed is None or self._packed_key != key:
+            dev = self.W_gate.device
+            if dev.type != "cuda":
+                raise RuntimeError("TauSparseMoE runs on CUDA only; move the module to a GPU")
+            H, E, G = self.hidden_size, self.num_experts, self.group_size
+            nbytes = _lib.load().ppmoe_packed_bytes(H, E, G)
+            if nbytes == 0:
+                raise _lib.PPMoEError("ppmoe_packed_bytes", -2, _lib.load().ppmoe_last_error().decode())
+            blob = torch.empty(nbytes + 1024, dtype=torch.uint8, device=dev)
+            off = (-blob.data_ptr()) % 1024
+            blob = blob[off:off + nbytes]
+            ws = [t.contiguous() for t in (self.W_gate, self.W_up, self.W_down, self.router)]
+            _lib.call("ppmoe_pack", *[t.data_ptr() for t in ws], H, E, G, blob.data_ptr(),
+                      _stream_handle(dev))
+            self._packed = blob
+            self._packed_key = key
+        return self._packed
+
+    def workspace(self, tokens: int) -> torch.Tensor:
+        dev = self.W_gate.device
+        tokens = min(max(tokens, 1), _lib.DECODE_MAX_TOKENS)
+        if self._ws is None or self._ws_tokens < tokens or self._ws.device != dev:
+            n = _lib.load().ppmoe_workspace_bytes(tokens, self.hidden_size, self.num_experts,
+                                                  self.group_size)
+            buf = torch.empty(n + 256, dtype=torch.uint8, device=dev)
+            off = (-buf.data_ptr()) % 256
+            ws = buf[off:off + n]
+            _lib.call("ppmoe_workspace_init", ws.data_ptr(), n, _stream_handle(dev))
+            self._ws, self._ws_tokens = ws, tokens
+        return self._ws
+
+    def check_device_status(self) -> None:
+        """Synchronise and raise if a kernel recorded a device-side error (bounded wait ran
+        out); clears the status word."""
+        if self._ws is not None:
+            _lib.call("ppmoe_workspace_status", self._ws.data_ptr(), _stream_handle(self._ws.device))
+
+    # ------------------------------------------------------------------ forward
+    def forward_decode(self, x_flat: torch.Tensor, *, logits_out=None, weights_out=None,
+                       pdl: bool = False) -> torch.Tensor:
+        N, H = x_flat.shape
+        out = torch.empty(N, H, dtype=torch.bfloat16, device=x_flat.device)
+        ws = self.workspace(N)
+        bias = self.logit_bias
+        if bias is not None:
+            bias = bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
+        counts = self.activated_statistics if self.track_statistics else None
+        _lib.call("ppmoe_decode", x_flat.data_ptr(), N, self.packed().data_ptr(), H,
+                  self.num_experts, self.group_size, float(self.tau), _lib.ptr(bias),
+                  out.data_ptr(), _lib.ptr(logits_out), _lib.ptr(weights_out), _lib.ptr(counts),
+                  ws.data_ptr(), ws.numel(), int(pdl), _stream_handle(x_flat.device))
+        return out
+
+    def forward_prefill(self, x_flat: torch.Tensor, **kw) -> torch.Tensor:
+        from . import prefill  # noqa: WPS433 (kept lazy: prefill owns large workspaces)
+        if self._prefill is None:
+            self._prefill = prefill.PrefillEngine(self)
+        return self._prefill(x_flat, **kw)
+
+    def forward(self, x: torch.Tensor, **kw) -> torch.Tensor:
+        B, L, H = x.shape
+        N = B * L
+        if x.device.type != "cuda":
+            raise RuntimeError("TauSparseMoE runs on CUDA only; got a tensor on " + str(x.device))
+        x_flat = x.reshape(N, H).to(torch.bfloat16).contiguous()
+        if N == 0:
+            return torch.empty(B, L, H, dtype=torch.bfloat16, device=x.device)
+        if N <= _lib.DECODE_MAX_TOKENS:
+            return self.forward_decode(x_flat, **kw).view(B, L, H)
+        return self.forward_prefill(x_flat, **kw).view(B, L, H)
+
+
+class IntegratedOpenPanguMoEMLP(nn.Module):
+    """Eval-mode stand-in for the reference MLP wrapper (src/openpangu_moe.py:43-130).
+
+    ``forward`` routes hidden states through ``self.tau_moe`` and unwraps a tuple as the
+    reference does (:125-130).  The training branch (dense projections + ``MoELayer``) is
+    not part of this library; calling the module in training mode raises.
+    """
+
+    def __init__(self, config, train_args, original_mlp=None, penalize_logits_list=None):
+        super().__init__()
+        hidden = getattr(config, "hidden_size", 1536)
+        inter = getattr(config, "intermediate_size", hidden * 4)
+        experts = inter // train_args.group_size
+        self.config, self.train_args = config, train_args
+        self.gate_proj = getattr(original_mlp, "gate_proj", None)
+        self.up_proj = getattr(original_mlp, "up_proj", None)
+        self.down_proj = getattr(original_mlp, "down_proj", None)
+        self.tau_moe = TauSparseMoE(hidden, inter, experts, train_args.group_size,
+                                    getattr(train_args, "tau", 0.5))
+
+    def forward(self, hidden_states, *args, **kwargs):
+        if self.training:
+            raise NotImplementedError("training-mode MoE routing is not provided by this library")
+        out = self.tau_moe(hidden_states)
+        return out[0] if isinstance(out, tuple) else out
+
+
+@torch.no_grad()
+def physical_reorder_for_inference(tau_moe: TauSparseMoE, gate_w, up_w, down_w, router_w,
+                                   experts_masks, tau: float) -> None:
+    """One layer of ``CustomOpenPangu.physical_reorder_for_inference``
+    (src/openpangu_moe.py:222-243): group neurons by expert and mount the transposed
+    projections on ``tau_moe``'s buffers.  ``gate_w/up_w [I,H]``, ``down_w [H,I]``,
+    ``router_w [E,H]`` are the ``nn.Linear`` weights, ``experts_masks [E,I]``."""
+    dev = tau_moe.W_gate.device
+    tau_moe.tau = tau
+    expert_ids = torch.argmax(experts_masks.to(torch.int32), dim=0)
+    sort_idx = torch.argsort(expert_ids, stable=True)
+    tau_moe.W_gate.data = gate_w[sort_idx, :].t().contiguous().to(device=dev, dtype=torch.bfloat16)
+    tau_moe.W_up.data = up_w[sort_idx, :].t().contiguous().to(device=dev, dtype=torch.bfloat16)
+    tau_moe.W_down.data = down_w[:, sort_idx].t().contiguous().to(device=dev, dtype=torch.bfloat16)
+    tau_moe.router.data = router_w.t().contiguous().to(device=dev, dtype=torch.bfloat16)
