@@ -11,7 +11,7 @@
  * `ppmoe_workspace_status()`.
  *
  * Shapes: hidden H, experts E, neurons per expert G, intermediate I = E * G.
- * Supported: H % 64 == 0, H <= 4096, 1 <= E <= 256, G % 8 == 0, G <= 256.
+ * Supported: H % 64 == 0, H <= 4096, E even and 2 <= E <= 256, G % 8 == 0, G <= 256.
  *
  * The reference exposes this path only as the PyTorch module `TauSparseMoE`
  * (src/tl_kernel_optimized_Ultimate_PanGU.py:468-615); each entry point below names the
@@ -103,6 +103,11 @@ PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hi
                  int group, float tau, const float* logit_bias, void* out, void* logits_out,
                  void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
                  void* stream);
+
+/* Diagnostics: when `buf` (device, >= 32 * 8 bytes per CTA of the decode grid) is non-NULL,
+ * later ppmoe_decode launches record per-CTA phase timestamps (SM clock64) into it; NULL
+ * switches recording off.  No counterpart in the reference (it has no tracing). */
+PPMOE_API void ppmoe_debug_trace(void* buf);
 
 #ifdef __cplusplus
 }

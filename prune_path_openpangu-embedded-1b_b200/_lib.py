@@ -34,6 +34,7 @@ SIGNATURES = {
     "ppmoe_workspace_status": (_c_int, [_c_void_p, _c_void_p]),
     "ppmoe_route_logits": (_c_int, [_c_void_p, _c_int, _c_int, _c_float, _c_void_p, _c_void_p,
                                     _c_void_p]),
+    "ppmoe_debug_trace": (None, [_c_void_p]),
     "ppmoe_decode": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                               _c_size_t, _c_int, _c_void_p]),

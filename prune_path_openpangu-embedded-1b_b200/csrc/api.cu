@@ -25,6 +25,8 @@ int route_logits_launch(const void*, int, int, float, const float*, void*, uint8
 int decode_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*,
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
 
+void decode_set_trace(void*);
+
 // Workspace header: status word, decode arrival counters; then the decode cluster partials.
 constexpr size_t kWsHeader = 256;
 constexpr size_t kWsCounters = 64;
@@ -37,8 +39,8 @@ static int check_shape(const char* fn, int H, int E, int G) {
     set_error("%s: hidden=%d must be a positive multiple of 64 <= 4096", fn, H);
     return PPMOE_ERR_UNSUPPORTED;
   }
-  if (E <= 0 || E > 256) {
-    set_error("%s: experts=%d must be in [1, 256]", fn, E);
+  if (E <= 0 || E > 256 || E % 2 != 0) {
+    set_error("%s: experts=%d must be even and in [2, 256]", fn, E);
     return PPMOE_ERR_UNSUPPORTED;
   }
   if (G <= 0 || G % 8 != 0 || G > 256) {
@@ -57,6 +59,8 @@ extern "C" {
 int ppmoe_version(void) { return 100; }
 
 const char* ppmoe_last_error(void) { return g_err; }
+
+void ppmoe_debug_trace(void* buf) { decode_set_trace(buf); }
 
 size_t ppmoe_packed_bytes(int hidden, int experts, int group) {
   if (check_shape("ppmoe_packed_bytes", hidden, experts, group)) return 0;

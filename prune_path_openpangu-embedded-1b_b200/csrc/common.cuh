@@ -74,6 +74,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -90,7 +94,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   const uint32_t a = smem_u32(bar);
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(a, parity)) return true;
-    if (i > 16) __nanosleep(64);
+    if (i > 4096) __nanosleep(32);
   }
   if (status) atomicOr(status, DEVERR_TIMEOUT);
   return false;

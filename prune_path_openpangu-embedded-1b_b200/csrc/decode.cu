@@ -58,7 +58,16 @@ struct DecodeArgs {
   uint32_t* status;
   int slots;           // ring depth
   int pdl;
+  unsigned long long* trace;  // optional per-CTA phase timestamps [grid][32] (diagnostics)
 };
+
+__device__ __forceinline__ unsigned long long clk64() {
+  unsigned long long c;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  return c;
+}
+#define PPMOE_TRACE(i) \
+  do { if (a.trace && threadIdx.x == 0) a.trace[blockIdx.x * 32 + (i)] = clk64(); } while (0)
 
 // Shared-memory carve-out (byte offsets from a 1 KiB aligned base).
 struct DecSmem {
@@ -107,6 +116,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   uint8_t* ring = smem + L.ring;
   const uint32_t rec_bytes = 3u * (uint32_t)H * 2u;
 
+  PPMOE_TRACE(0);
   // ---- prologue: barriers; router slice prefetch (weights only: legal before the PDL wait)
   if (tid == 0) {
     for (int s = 0; s <= a.slots; ++s) mbar_init(&bars[s], 1);
@@ -126,35 +136,52 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   for (int i = N * H + tid; i < NT * H; i += kDecThreads) xs[i] = __float2bfloat16_rn(0.f);
   for (int i = tid; i < E; i += kDecThreads) tokmask[i] = 0u;
   mbar_wait(bar_in, 0, a.status);
+  PPMOE_TRACE(1);
 
-  // ---- 1. router partial over this rank's K-slice: thread (group g, expert e)
+  // ---- 1. router partial over this rank's K-slice.  The E/2 expert pairs are split into
+  // PB blocks of 32 (lane = pair within block); warp w takes pair block w % PB and rows
+  // k = g, g + KG, ... with g = w / PB.  The KG row-group partials are then summed in group
+  // order, so the operation order is fixed.
   {
-    const int KG = max(1, kDecThreads / E);
-    const int g = tid / E, e = tid - g * E;
-    float acc[NT];
+    const int E2 = E >> 1;
+    const int PB = (E2 + 31) >> 5;
+    const int KG = max(1, kDecWarps / PB);
+    float* scratch = reinterpret_cast<float*>(ring + align_up(rs_bytes, 128));  // [KG][NT][E]
+    const __nv_bfloat162* rs2 = reinterpret_cast<const __nv_bfloat162*>(rs);
+    const int pb = warp % PB, g = warp / PB;
+    const int ep = pb * 32 + lane;
+    if (g < KG && ep < E2) {
+      float2 acc[NT];
 #pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-    if (g < KG) {
+      for (int t = 0; t < NT; ++t) acc[t] = make_float2(0.f, 0.f);
+#pragma unroll 4
       for (int k = g; k < HS; k += KG) {
-        const float r = __bfloat162float(rs[(size_t)k * E + e]);
+        const float2 r = __bfloat1622float2(rs2[(size_t)k * E2 + ep]);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = fmaf(__bfloat162float(xs[t * H + rank * HS + k]), r, acc[t]);
+        for (int t = 0; t < NT; ++t) {
+          const float xv = __bfloat162float(xs[t * H + rank * HS + k]);
+          acc[t].x = fmaf(xv, r.x, acc[t].x);
+          acc[t].y = fmaf(xv, r.y, acc[t].y);
+        }
       }
-    }
-    // fixed-order combine of the KG groups through the (still free) ring tail
-    float* scratch = reinterpret_cast<float*>(ring + align_up(rs_bytes, 128));
-    if (g < KG) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t) scratch[(g * NT + t) * E + e] = acc[t];
+      for (int t = 0; t < NT; ++t)
+        *reinterpret_cast<float2*>(scratch + (g * NT + t) * E + 2 * ep) = acc[t];
     }
     __syncthreads();
     for (int i = tid; i < NT * E; i += kDecThreads) {
+      float v[kDecWarps];
+#pragma unroll
+      for (int q = 0; q < kDecWarps; ++q) v[q] = q < KG ? scratch[q * NT * E + i] : 0.f;
       float s = 0.f;
-      for (int q = 0; q < KG; ++q) s += scratch[q * NT * E + i];
+#pragma unroll
+      for (int q = 0; q < kDecWarps; ++q) s += v[q];  // group order; trailing zeros are exact
       part[i] = s;
     }
   }
+  PPMOE_TRACE(2);
   cluster.sync();  // partials visible cluster-wide
+  PPMOE_TRACE(3);
 
   // ---- full logits: sum the 8 rank partials in rank order
   for (int i = tid; i < N * E; i += kDecThreads) {
@@ -166,6 +193,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     lg[i] = l;
   }
   __syncthreads();
+  PPMOE_TRACE(4);
 
   // ---- 2. selection, one warp per token
   for (int t = warp; t < N; t += kDecWarps) {
@@ -186,7 +214,29 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   __syncthreads();
-  // union list in ascending expert order (warp 0, ballot compaction)
+  PPMOE_TRACE(5);
+
+  // ---- 3. experts.  The union's neurons (|U| * G) are split evenly over the grid; CTA
+  // neuron n lives in ring slot n % slots.  Warp 0 builds the union list (ascending expert
+  // order, ballot compaction) and issues the first window: one bulk copy per run of neurons
+  // that share an expert (contiguous in the packed blob and in the ring), completing on the
+  // run head's barrier; the other slots of the run get a plain arrival so that every slot
+  // barrier has finished exactly one phase before refills start.
+  const uint64_t pol = policy_evict_first();
+  int i0 = 0, cnt = 0;
+  auto work_range = [&](int nU) {
+    const int W = nU * G;
+    i0 = (int)((long long)W * blockIdx.x / gridDim.x);
+    cnt = (int)((long long)W * (blockIdx.x + 1) / gridDim.x) - i0;
+  };
+  auto issue_neuron = [&](int n) {  // one record into slot n % slots
+    const int gi = i0 + n;
+    const int u = gi / G, j = gi - u * G;
+    const int sl = n % a.slots;
+    mbar_arrive_expect_tx(&bars[sl], rec_bytes);
+    bulk_g2s(ring + (size_t)sl * rec_bytes, a.experts + ((size_t)ulist[u] * G + j) * 3 * H, rec_bytes,
+             &bars[sl], pol);
+  };
   if (warp == 0) {
     int base = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
@@ -197,6 +247,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       base += __popc(b);
     }
     if (lane == 0) misc[0] = base;
+    __syncwarp();
+    work_range(base);
+    // the router slice / scratch in the ring is dead: every warp passed the barrier above
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const int win = min(cnt, a.slots);
+    for (int n = lane; n < win; n += 32) {
+      const int gi = i0 + n;
+      const int u = gi / G, j = gi - u * G;
+      if (n == 0 || j == 0) {
+        const int len = min(G - j, win - n);
+        mbar_arrive_expect_tx(&bars[n], (uint32_t)len * rec_bytes);
+        bulk_g2s(ring + (size_t)n * rec_bytes, a.experts + ((size_t)ulist[u] * G + j) * 3 * H,
+                 (uint32_t)len * rec_bytes, &bars[n], pol);
+      } else {
+        mbar_arrive(&bars[n]);
+      }
+    }
   }
   // optional side outputs from the first CTA of the grid
   if (blockIdx.x == 0) {
@@ -213,26 +280,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   __syncthreads();
-
-  // ---- 3. experts: this CTA's neuron range of the union
-  const int nU = misc[0];
-  const long long W = (long long)nU * G;
-  const long long i0 = W * blockIdx.x / gridDim.x, i1 = W * (blockIdx.x + 1) / gridDim.x;
-  const int cnt = (int)(i1 - i0);
-  const uint64_t pol = policy_evict_first();
-  auto issue = [&](int n) {  // neuron n of this CTA -> slot n % slots
-    const long long gi = i0 + n;
-    const int e = ulist[gi / G], j = (int)(gi % G);
-    const int s = n % a.slots;
-    mbar_arrive_expect_tx(&bars[s], rec_bytes);
-    bulk_g2s(ring + (size_t)s * rec_bytes, a.experts + ((size_t)e * G + j) * 3 * H, rec_bytes, &bars[s], pol);
-  };
-  // the router slice / scratch in the ring must be dead before the first record lands
-  __syncthreads();
-  if (tid == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (int n = 0; n < min(cnt, a.slots); ++n) issue(n);
-  }
+  if (warp != 0) work_range(misc[0]);
+  PPMOE_TRACE(6);
 
   float acc[HCH][NT][4];
 #pragma unroll
@@ -242,6 +291,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[c][t][q] = 0.f;
 
+  // Wait for every run of the first window before any slot is refilled: a run's records are
+  // signalled on its head slot's barrier, which is re-armed once that slot is refilled.
+  {
+    const int win = min(cnt, a.slots);
+    for (int n = 0; n < win;) {
+      mbar_wait(&bars[n], 0u, a.status);
+      n += G - (i0 + n) % G;
+    }
+  }
+  PPMOE_TRACE(7);
+
   for (int b0 = 0; b0 < cnt; b0 += kDecWarps) {
     const int n = b0 + warp;
 #pragma unroll
@@ -250,17 +310,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     __syncwarp();
     if (n < cnt) {
       const int s = n % a.slots;
-      mbar_wait(&bars[s], (uint32_t)((n / a.slots) & 1), a.status);
-      const long long gi = i0 + n;
-      const int u = (int)(gi / G);
-      const int e = ulist[u];
+      if (n >= a.slots) mbar_wait(&bars[s], (uint32_t)((n / a.slots) & 1), a.status);
+      const int e = ulist[(i0 + n) / G];
       uint32_t tm = tokmask[e];
       const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes);
       const __nv_bfloat16* up = gate + H;
       while (tm) {
         const int t = __ffs(tm) - 1;
         tm &= tm - 1u;
-        float sg = 0.f, su = 0.f;
+        // four independent accumulators per row keep the FMA chains short
+        float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
         for (int v = lane; v < H / 8; v += 32) {
           const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + v * 8);
           const uint4 gv = *reinterpret_cast<const uint4*>(gate + v * 8);
@@ -273,14 +333,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
             const float2 xf = __bfloat1622float2(xp[q]);
             const float2 gf = __bfloat1622float2(gp[q]);
             const float2 uf = __bfloat1622float2(up2[q]);
-            sg = fmaf(xf.x, gf.x, sg); sg = fmaf(xf.y, gf.y, sg);
-            su = fmaf(xf.x, uf.x, su); su = fmaf(xf.y, uf.y, su);
+            sg[q] = fmaf(xf.y, gf.y, fmaf(xf.x, gf.x, sg[q]));
+            su[q] = fmaf(xf.y, uf.y, fmaf(xf.x, uf.x, su[q]));
           }
         }
-        sg = warp_sum(sg);
-        su = warp_sum(su);
+        float g2 = (sg[0] + sg[1]) + (sg[2] + sg[3]);
+        float u2 = (su[0] + su[1]) + (su[2] + su[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          g2 += __shfl_xor_sync(0xffffffffu, g2, o);
+          u2 += __shfl_xor_sync(0xffffffffu, u2, o);
+        }
         if (lane == 0) {
-          const float gb = bf16r(sg), ub = bf16r(su);
+          const float gb = bf16r(g2), ub = bf16r(u2);
           const float sb = bf16r(__fdiv_rn(gb, 1.f + expf(-gb)));
           const float ab = bf16r(sb * ub);
           a2s[warp * NT + t] = bf16r(ab * ws[t * E + e]);
@@ -288,38 +353,47 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       }
     }
     __syncthreads();
-    // down rows of this batch into the fp32 accumulators
     const int nb = min(kDecWarps, cnt - b0);
-    for (int m = 0; m < nb; ++m) {
-      const int s = (b0 + m) % a.slots;
-      const __nv_bfloat16* down = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes) + 2 * H;
-      float av[NT];
-#pragma unroll
-      for (int t = 0; t < NT; ++t) av[t] = a2s[m * NT + t];
+    // down rows of this batch, four per step: loads first, then the dependent FMAs
+    for (int m0 = 0; m0 < nb; m0 += 4) {
 #pragma unroll
       for (int c = 0; c < HCH; ++c) {
         const int h4 = tid + c * kDecThreads;
         if (h4 < H / 4) {
-          const uint2 dv = *reinterpret_cast<const uint2*>(down + h4 * 4);
-          const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.x));
-          const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.y));
+          uint2 dv[4];
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            acc[c][t][0] = fmaf(av[t], d01.x, acc[c][t][0]);
-            acc[c][t][1] = fmaf(av[t], d01.y, acc[c][t][1]);
-            acc[c][t][2] = fmaf(av[t], d23.x, acc[c][t][2]);
-            acc[c][t][3] = fmaf(av[t], d23.y, acc[c][t][3]);
+          for (int q = 0; q < 4; ++q) {
+            const int m = min(m0 + q, nb - 1);
+            const __nv_bfloat16* down =
+                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)((b0 + m) % a.slots) * rec_bytes) + 2 * H;
+            dv[q] = *reinterpret_cast<const uint2*>(down + h4 * 4);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (m0 + q < nb) {
+              const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].x));
+              const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].y));
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const float av = a2s[(m0 + q) * NT + t];
+                acc[c][t][0] = fmaf(av, d01.x, acc[c][t][0]);
+                acc[c][t][1] = fmaf(av, d01.y, acc[c][t][1]);
+                acc[c][t][2] = fmaf(av, d23.x, acc[c][t][2]);
+                acc[c][t][3] = fmaf(av, d23.y, acc[c][t][3]);
+              }
+            }
           }
         }
       }
     }
     __syncthreads();
-    if (tid == 0) {
+    if (warp == 0) {  // refill the slots this batch released
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int m = 0; m < nb; ++m)
-        if (b0 + m + a.slots < cnt) issue(b0 + m + a.slots);
+      const int lo = b0 + a.slots, hi = min(cnt, b0 + nb + a.slots);
+      for (int n2 = lo + lane; n2 < hi; n2 += 32) issue_neuron(n2);
     }
   }
+  PPMOE_TRACE(8);
   if (a.pdl) pdl_launch_dependents();
 
   // ---- 4a. CTA partial -> shared (ring is idle: every issued record has been consumed)
@@ -336,34 +410,45 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   cluster.sync();
+  PPMOE_TRACE(9);
   // ---- 4b. cluster partial of this rank's column slice, rank order
   for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
     const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
+    float4 v[kCluster];
+#pragma unroll
+    for (int q = 0; q < kCluster; ++q)
+      v[q] = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, q) + (size_t)t * H + h);
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int q = 0; q < kCluster; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(cluster.map_shared_rank(red, q) + (size_t)t * H + h);
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-    }
+    for (int q = 0; q < kCluster; ++q) { s.x += v[q].x; s.y += v[q].y; s.z += v[q].z; s.w += v[q].w; }
     *reinterpret_cast<float4*>(a.cpart + ((size_t)cid * N + t) * H + h) = s;
   }
-  cluster.sync();  // peers finished reading this CTA's shared memory
-  // ---- 4c. last cluster to finish this slice sums all cluster partials
-  __threadfence();
+  // peers may still read this CTA's shared memory: arrive now, wait before exiting
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  // ---- 4c. the last cluster to finish this column slice sums all cluster partials
   __syncthreads();
   if (tid == 0) {
+    __threadfence();
     const uint32_t old = atomicAdd(&a.counters[rank], 1u);
     misc[1] = (old == (uint32_t)nclusters - 1u);
   }
   __syncthreads();
+  PPMOE_TRACE(10);
   if (misc[1]) {
     __threadfence();
     for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
       const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
+      // eight independent L2 reads in flight per round; additions stay in cluster order
       float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = 0; c < nclusters; ++c) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.cpart + ((size_t)c * N + t) * H + h));
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      for (int c0 = 0; c0 < nclusters; c0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (c0 + c < nclusters)
+            v[c] = __ldcg(reinterpret_cast<const float4*>(a.cpart + ((size_t)(c0 + c) * N + t) * H + h));
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (c0 + c < nclusters) { s.x += v[c].x; s.y += v[c].y; s.z += v[c].z; s.w += v[c].w; }
       }
       __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
       uint2 pk;
@@ -373,6 +458,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
     if (tid == 0) a.counters[rank] = 0u;  // re-arm for the next launch
   }
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  PPMOE_TRACE(11);
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 30] = (unsigned long long)cnt;
 }
 
 // ------------------------------------------------------------------ host side
@@ -395,6 +483,8 @@ struct DecodeCfgCache {
   int clusters = 0;
 };
 static thread_local DecodeCfgCache g_dec_cache;
+static unsigned long long* g_trace = nullptr;
+void decode_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(buf); }
 
 int decode_launch(const void* x, int tokens, const void* packed, int H, int E, int G, float tau,
                   const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
@@ -419,7 +509,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
     while (slots > 2 && L.total + 1024 > (uint32_t)max_optin) L = dec_smem(NT, H, E, --slots);
     // the router slice and its group scratch alias the ring
     const size_t need_ring = align_up((size_t)(H / kCluster) * E * 2, 128) +
-                             (size_t)max(1, kDecThreads / E) * NT * E * 4;
+                             (size_t)max(1, kDecWarps / ((E / 2 + 31) / 32)) * NT * E * 4;
     const size_t red_ring = (size_t)NT * H * 4;
     if ((size_t)slots * 3 * H * 2 < need_ring || (size_t)slots * 3 * H * 2 < red_ring ||
         L.total + 1024 > (uint32_t)max_optin || slots < 2) {
@@ -472,6 +562,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
   a.status = status;
   a.slots = C.slots;
   a.pdl = pdl;
+  a.trace = g_trace;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];

@@ -2,15 +2,14 @@
 //
 // Restates src/MoEBlock.py:68-91 (softmax_thresholding) with the rounding points of the
 // reference's CPU bf16 path:
-//   p_e  = bf16( exp(l_e - max) / sum_e exp(l_e - max) )      (fp32 inside)
+//   p_e  = bf16( exp(l_e - max) * (1 / sum_e exp(l_e - max)) ) (fp32 inside)
 //   order: p descending, ties -> lower expert index          (stable sort contract; the
 //          reference Triton decode kernel picks the lowest index too, tl:368-369)
 //   c_j  = bf16( p_(0) + ... + p_(j) )                       (sequential fp32 sum)
 //   keep expert (j) iff c_j < bf16(tau)  or  j == 0          (forced top-1, MoEBlock.py:81-86)
 //   w_e  = bf16( 1 / (1 + exp(-l_e)) ) on kept experts, 0 elsewhere.
-// The cumulative sum is monotone, so the first rejected rank ends the selection; the
-// selection loop is an iterative warp arg-max (one 64-bit max-reduction per kept expert),
-// which visits experts in exactly the sorted order without sorting all of them.
+// The cumulative sum is monotone, so the kept experts are a prefix of the sorted order.
+// Requires E <= 256 (8 experts per lane; the 16-bit index field needs E < 65535).
 #pragma once
 #include "common.cuh"
 
@@ -18,59 +17,177 @@ namespace ppmoe {
 
 constexpr int kMaxExpertsPerLane = 8;  // E <= 256
 
-// l[i] holds the bf16-valued logit of expert e = lane + 32*i (i < epl, e < E).
-// On return w[i] is the gate weight (0 when not selected) and the returned bitmask has
-// bit i set when expert lane + 32*i was selected.
-__device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
-                                                        float tau_b, float (&w)[kMaxExpertsPerLane]) {
+__device__ __forceinline__ uint32_t float_order_key(float f) {  // unsigned order == float order
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float float_from_order_key(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Sequential selection over 32-bit keys (bf16 bits of p << 16 | 0xFFFF - e): one redux.sync
+// max per kept expert, which visits experts in exactly the sorted order.  Exact for any
+// probabilities; used when the parallel path's exactness condition does not hold.
+__device__ __forceinline__ uint32_t select_sequential(uint32_t (&key)[kMaxExpertsPerLane], int E, float tau_b) {
   const int lane = threadIdx.x & 31;
-  const int epl = (E + 31) >> 5;
-  float m = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i)
-    if (i < epl && lane + 32 * i < E) m = fmaxf(m, l[i]);
-  m = warp_max(m);
-  float ex[kMaxExpertsPerLane];
-  float s = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    ex[i] = (i < epl && lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
-    s += ex[i];
-  }
-  s = warp_sum(s);
-  unsigned long long key[kMaxExpertsPerLane];
-#pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    const int e = lane + 32 * i;
-    if (i < epl && e < E) {
-      const float p = bf16r(__fdiv_rn(ex[i], s));  // p >= 0: its bit pattern orders like p
-      key[i] = (static_cast<unsigned long long>(__float_as_uint(p)) << 32) |
-               static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(e));
-    } else {
-      key[i] = 0ull;  // never selected (below every real key)
-    }
-  }
   uint32_t bits = 0;
   float cum = 0.f;
   for (int j = 0; j < E; ++j) {
-    unsigned long long k = 0ull;
+    uint32_t k = 0u;
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) k = key[i] > k ? key[i] : k;
-    k = warp_max_u64(k);
-    const float p = __uint_as_float(static_cast<uint32_t>(k >> 32));
-    const int e = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) k = max(k, key[i]);
+    k = __reduce_max_sync(0xffffffffu, k);
+    const float p = __uint_as_float(k & 0xFFFF0000u);
+    const int e = static_cast<int>(0xFFFFu - (k & 0xFFFFu));
     cum += p;
     if (j > 0 && !(bf16r(cum) < tau_b)) break;
     if ((e & 31) == lane) {
       const int i = e >> 5;
 #pragma unroll
       for (int q = 0; q < kMaxExpertsPerLane; ++q)
-        if (q == i) { key[q] = 0ull; bits |= 1u << q; }
+        if (q == i) { key[q] = 0u; bits |= 1u << q; }
     }
   }
+  return bits;
+}
+
+// Parallel selection: warp bitonic sort of the keys (descending), prefix sums of the sorted
+// probabilities, cutoff by a min-reduction.  Every probability is a bf16 value; when each
+// one up to the cutoff is 0 or >= 2^-16 and the sums stay below 2, every partial sum is a
+// multiple of 2^-23 below 2 and therefore exact in fp32, so any summation order gives the
+// sequential sums bit for bit.  Otherwise returns false (warp-uniformly) and the caller
+// falls back to select_sequential.
+template <int EPL>
+__device__ __forceinline__ bool select_parallel(const uint32_t (&key)[kMaxExpertsPerLane], int E, float tau_b,
+                                                uint32_t& bits_out) {
+  const int lane = threadIdx.x & 31;
+  constexpr int n = 32 * EPL;
+  uint32_t v[EPL];
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) v[r] = key[r];
+  // element index i = lane * EPL + r
+#pragma unroll
+  for (int k = 2; k <= n; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= EPL) {
+        const int lj = j / EPL;
+#pragma unroll
+        for (int r = 0; r < EPL; ++r) {
+          const int i = lane * EPL + r;
+          const uint32_t o = __shfl_xor_sync(0xffffffffu, v[r], lj);
+          const bool keep_max = ((i & k) == 0) == ((i & j) == 0);
+          v[r] = keep_max ? max(v[r], o) : min(v[r], o);
+        }
+      } else {
+#pragma unroll
+        for (int r = 0; r < EPL; ++r) {
+          const int rp = r ^ j;
+          if (rp > r) {
+            const int i = lane * EPL + r;
+            const uint32_t a = v[r], b = v[rp];
+            const bool desc = (i & k) == 0;
+            v[r] = desc ? max(a, b) : min(a, b);
+            v[rp] = desc ? min(a, b) : max(a, b);
+          }
+        }
+      }
+    }
+  }
+  float loc[EPL];
+  float run = 0.f;
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) {
+    run += __uint_as_float(v[r] & 0xFFFF0000u);
+    loc[r] = run;
+  }
+  float incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const float excl = incl - run;  // exact under the condition checked below
+  uint32_t keep_lane = 0;
+  int first_rej = n;
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) {
+    const int i = lane * EPL + r;
+    const bool keep = i < E && (i == 0 || bf16r(excl + loc[r]) < tau_b);
+    keep_lane |= (uint32_t)keep << r;
+    if (!keep && i < first_rej) first_rej = i;
+  }
+  const int J = __reduce_min_sync(0xffffffffu, first_rej);  // sums up to index J decide
+  uint32_t bad = excl + loc[EPL - 1] >= 2.f;
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) {
+    const int i = lane * EPL + r;
+    const float p = __uint_as_float(v[r] & 0xFFFF0000u);
+    if (i <= J && i < E && p != 0.f && p < 1.52587890625e-05f) bad = 1;  // 2^-16
+  }
+  if (__any_sync(0xffffffffu, bad)) return false;
+  // kept experts -> per-owner-lane bits (expert e is owned by lane e % 32, slot e / 32)
+  uint32_t bits = 0;
+#pragma unroll
+  for (int q = 0; q < kMaxExpertsPerLane; ++q) {
+    if (q * 32 < E) {
+      uint32_t wq = 0u;
+#pragma unroll
+      for (int r = 0; r < EPL; ++r) {
+        const uint32_t e = 0xFFFFu - (v[r] & 0xFFFFu);
+        wq |= (((keep_lane >> r) & 1u) && (e >> 5) == (uint32_t)q) ? (1u << (e & 31u)) : 0u;
+      }
+      wq = __reduce_or_sync(0xffffffffu, wq);
+      bits |= ((wq >> lane) & 1u) << q;
+    }
+  }
+  bits_out = bits;
+  return true;
+}
+
+// l[i] holds the bf16-valued logit of expert e = lane + 32*i (e < E).  On return w[i] is the
+// gate weight (0 when not selected) and the returned bitmask has bit i set when expert
+// lane + 32*i was selected.  Each probability is a bf16 value, so its fp32 bit pattern has
+// 16 zero low bits; the 32-bit key (bf16 bits of p) << 16 | (0xFFFF - e) orders candidates
+// by p descending and then by expert index ascending.
+__device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
+                                                        float tau_b, float (&w)[kMaxExpertsPerLane]) {
+  const int lane = threadIdx.x & 31;
+  uint32_t mk = 0u;
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i)
-    w[i] = (bits >> i) & 1u ? bf16r(__fdiv_rn(1.f, 1.f + expf(-l[i]))) : 0.f;
+    if (lane + 32 * i < E) mk = max(mk, float_order_key(l[i]));
+  const float m = float_from_order_key(__reduce_max_sync(0xffffffffu, mk));
+  float ex[kMaxExpertsPerLane];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    ex[i] = (lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
+    s += ex[i];
+  }
+  s = warp_sum(s);
+  const float rs = __frcp_rn(s);
+  uint32_t key[kMaxExpertsPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      const float p = bf16r(__fmul_rn(ex[i], rs));  // p >= 0: its bit pattern orders like p
+      key[i] = (__float_as_uint(p) & 0xFFFF0000u) | (0xFFFFu - static_cast<uint32_t>(e));
+    } else {
+      key[i] = 0u;  // never selected (below every real key)
+    }
+  }
+  uint32_t bits = 0;
+  bool done;
+  if (E <= 32) done = select_parallel<1>(key, E, tau_b, bits);
+  else if (E <= 64) done = select_parallel<2>(key, E, tau_b, bits);
+  else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
+  else done = select_parallel<8>(key, E, tau_b, bits);
+  if (!done) bits = select_sequential(key, E, tau_b);
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i)
+    w[i] = (bits >> i) & 1u ? bf16r(__frcp_rn(1.f + expf(-l[i]))) : 0.f;
   return bits;
 }
 
