@@ -92,6 +92,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // every cluster barrier and the launch ends.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
   const uint32_t a = smem_u32(bar);
+#pragma unroll 1
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if (i > 4096) __nanosleep(32);

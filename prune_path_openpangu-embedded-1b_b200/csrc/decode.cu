@@ -85,7 +85,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   s.tokmask = o; o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.ulist = o;   o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
-  s.a2 = o;      o = (uint32_t)align_up(o + (size_t)kDecWarps * NT * 4, 1024);
+  s.a2 = o;      o = (uint32_t)align_up(o + (size_t)64 * NT * 4, 1024);  // >= max(warps, slots)
   s.ring = o;    o += (uint32_t)slots * 3u * (uint32_t)H * 2u;
   s.total = o;
   return s;
@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   if (a.pdl) pdl_wait();
   if (tid == 0) bulk_g2s(xs, a.x, x_bytes, bar_in, policy_evict_first());
   // zero-fill padded token rows so the router partials stay finite
+  #pragma unroll 1
   for (int i = N * H + tid; i < NT * H; i += kDecThreads) xs[i] = __float2bfloat16_rn(0.f);
+  #pragma unroll 1
   for (int i = tid; i < E; i += kDecThreads) tokmask[i] = 0u;
   mbar_wait(bar_in, 0, a.status);
   PPMOE_TRACE(1);
@@ -169,6 +171,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         *reinterpret_cast<float2*>(scratch + (g * NT + t) * E + 2 * ep) = acc[t];
     }
     __syncthreads();
+    #pragma unroll 1
     for (int i = tid; i < NT * E; i += kDecThreads) {
       float v[kDecWarps];
 #pragma unroll
@@ -184,6 +187,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   PPMOE_TRACE(3);
 
   // ---- full logits: sum the 8 rank partials in rank order
+  #pragma unroll 1
   for (int i = tid; i < N * E; i += kDecThreads) {
     float s = 0.f;
 #pragma unroll
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   PPMOE_TRACE(4);
 
   // ---- 2. selection, one warp per token
+  #pragma unroll 1
   for (int t = warp; t < N; t += kDecWarps) {
     float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
 #pragma unroll
@@ -239,6 +244,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   };
   if (warp == 0) {
     int base = 0;
+    #pragma unroll 1
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
       const bool on = e < E && tokmask[e] != 0u;
@@ -252,6 +258,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     // the router slice / scratch in the ring is dead: every warp passed the barrier above
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     const int win = min(cnt, a.slots);
+    #pragma unroll 1
     for (int n = lane; n < win; n += 32) {
       const int gi = i0 + n;
       const int u = gi / G, j = gi - u * G;
@@ -267,13 +274,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   }
   // optional side outputs from the first CTA of the grid
   if (blockIdx.x == 0) {
+    #pragma unroll 1
     for (int i = tid; i < N * E; i += kDecThreads) {
       if (a.logits_out) a.logits_out[i] = __float2bfloat16_rn(lg[i]);
       if (a.weights_out) a.weights_out[i] = __float2bfloat16_rn(ws[i]);
     }
     if (a.counts) {
+      #pragma unroll 1
       for (int e = tid; e < E; e += kDecThreads) {
         long long c = 0;
+        #pragma unroll 1
         for (int t = 0; t < N; ++t) c += ws[t * E + e] > 0.f;
         a.counts[e] += c;
       }
@@ -295,6 +305,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   // signalled on its head slot's barrier, which is re-armed once that slot is refilled.
   {
     const int win = min(cnt, a.slots);
+    #pragma unroll 1
     for (int n = 0; n < win;) {
       mbar_wait(&bars[n], 0u, a.status);
       n += G - (i0 + n) % G;
@@ -302,7 +313,92 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   }
   PPMOE_TRACE(7);
 
-  for (int b0 = 0; b0 < cnt; b0 += kDecWarps) {
+  // Single-token fast path, whole window resident: every warp takes neurons w, w+12, ...
+  // two at a time with the token's activations held in registers, one barrier, then every
+  // thread applies all down rows to its output columns.
+  bool fast = false;
+  if constexpr (NT == 1) fast = cnt <= a.slots && H <= 2048;
+  if (fast) {
+    constexpr int VQ = 8;  // H / 8 vectors per row, 32 lanes -> <= 8 per lane at H <= 2048
+    uint4 xr[VQ];
+#pragma unroll
+    for (int q = 0; q < VQ; ++q) {
+      const int v = lane + 32 * q;
+      xr[q] = v < H / 8 ? *reinterpret_cast<const uint4*>(xs + v * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll 1
+    for (int n0 = warp; n0 < cnt; n0 += 2 * kDecWarps) {
+      const int n1 = n0 + kDecWarps;
+      const bool two = n1 < cnt;
+      const __nv_bfloat16* g0 = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)n0 * rec_bytes);
+      const __nv_bfloat16* g1 = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)(two ? n1 : n0) * rec_bytes);
+      float acc4[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // g0 u0 g1 u1
+#pragma unroll
+      for (int q = 0; q < VQ; ++q) {
+        const int v = lane + 32 * q;
+        if (v < H / 8) {
+          const __nv_bfloat16* rowp[4] = {g0, g0 + H, g1, g1 + H};
+          const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xr[q]);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(rowp[r] + v * 8);
+            const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+            for (int h2 = 0; h2 < 4; ++h2) {
+              const float2 xf = __bfloat1622float2(xp[h2]);
+              const float2 wf = __bfloat1622float2(wp[h2]);
+              acc4[r][h2 & 1] = fmaf(xf.y, wf.y, fmaf(xf.x, wf.x, acc4[r][h2 & 1]));
+            }
+          }
+        }
+      }
+      float d[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) d[r] = acc4[r][0] + acc4[r][1];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) d[r] += __shfl_xor_sync(0xffffffffu, d[r], o);
+      if (lane < 2 && (lane == 0 || two)) {
+        const int n = lane == 0 ? n0 : n1;
+        const float gb = bf16r(d[2 * lane]), ub = bf16r(d[2 * lane + 1]);
+        const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+        const float ab = bf16r(sb * ub);
+        a2s[n] = bf16r(ab * ws[ulist[(i0 + n) / G]]);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < HCH; ++c) {
+      const int h4 = tid + c * kDecThreads;
+      if (h4 < H / 4) {
+#pragma unroll 1
+        for (int m0 = 0; m0 < cnt; m0 += 4) {
+          uint2 dv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int m = min(m0 + q, cnt - 1);
+            dv[q] = *reinterpret_cast<const uint2*>(
+                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)m * rec_bytes) + 2 * H + h4 * 4);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (m0 + q < cnt) {
+              const float av = a2s[m0 + q];
+              const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].x));
+              const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].y));
+              acc[c][0][0] = fmaf(av, d01.x, acc[c][0][0]);
+              acc[c][0][1] = fmaf(av, d01.y, acc[c][0][1]);
+              acc[c][0][2] = fmaf(av, d23.x, acc[c][0][2]);
+              acc[c][0][3] = fmaf(av, d23.y, acc[c][0][3]);
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int b0 = 0; b0 < (fast ? 0 : cnt); b0 += kDecWarps) {
     const int n = b0 + warp;
 #pragma unroll
     for (int t = 0; t < NT; ++t)
@@ -315,6 +411,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       uint32_t tm = tokmask[e];
       const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes);
       const __nv_bfloat16* up = gate + H;
+      #pragma unroll 1
       while (tm) {
         const int t = __ffs(tm) - 1;
         tm &= tm - 1u;
@@ -346,7 +443,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         }
         if (lane == 0) {
           const float gb = bf16r(g2), ub = bf16r(u2);
-          const float sb = bf16r(__fdiv_rn(gb, 1.f + expf(-gb)));
+          const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
           const float ab = bf16r(sb * ub);
           a2s[warp * NT + t] = bf16r(ab * ws[t * E + e]);
         }
@@ -390,6 +487,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     if (warp == 0) {  // refill the slots this batch released
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       const int lo = b0 + a.slots, hi = min(cnt, b0 + nb + a.slots);
+      #pragma unroll 1
       for (int n2 = lo + lane; n2 < hi; n2 += 32) issue_neuron(n2);
     }
   }
@@ -412,6 +510,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   cluster.sync();
   PPMOE_TRACE(9);
   // ---- 4b. cluster partial of this rank's column slice, rank order
+  #pragma unroll 1
   for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
     const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
     float4 v[kCluster];
@@ -436,10 +535,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   PPMOE_TRACE(10);
   if (misc[1]) {
     __threadfence();
+    #pragma unroll 1
     for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
       const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
       // eight independent L2 reads in flight per round; additions stay in cluster order
       float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      #pragma unroll 1
       for (int c0 = 0; c0 < nclusters; c0 += 8) {
         float4 v[8];
 #pragma unroll

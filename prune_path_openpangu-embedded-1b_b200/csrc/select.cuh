@@ -65,10 +65,11 @@ __device__ __forceinline__ bool select_parallel(const uint32_t (&key)[kMaxExpert
   uint32_t v[EPL];
 #pragma unroll
   for (int r = 0; r < EPL; ++r) v[r] = key[r];
-  // element index i = lane * EPL + r
-#pragma unroll
+  // element index i = lane * EPL + r.  The stage loops stay rolled: this code runs once per
+  // token and its size (instruction-cache misses) matters more than loop overhead.
+#pragma unroll 1
   for (int k = 2; k <= n; k <<= 1) {
-#pragma unroll
+#pragma unroll 1
     for (int j = k >> 1; j > 0; j >>= 1) {
       if (j >= EPL) {
         const int lj = j / EPL;
@@ -81,14 +82,19 @@ __device__ __forceinline__ bool select_parallel(const uint32_t (&key)[kMaxExpert
         }
       } else {
 #pragma unroll
-        for (int r = 0; r < EPL; ++r) {
-          const int rp = r ^ j;
-          if (rp > r) {
-            const int i = lane * EPL + r;
-            const uint32_t a = v[r], b = v[rp];
-            const bool desc = (i & k) == 0;
-            v[r] = desc ? max(a, b) : min(a, b);
-            v[rp] = desc ? min(a, b) : max(a, b);
+        for (int jj = 1; jj < EPL; jj <<= 1) {  // j < EPL: exchange inside the lane
+          if (jj == j) {
+#pragma unroll
+            for (int r = 0; r < EPL; ++r) {
+              const int rp = r ^ jj;
+              if (rp > r) {
+                const int i = lane * EPL + r;
+                const uint32_t a = v[r], b = v[rp];
+                const bool desc = (i & k) == 0;
+                v[r] = desc ? max(a, b) : min(a, b);
+                v[rp] = desc ? min(a, b) : max(a, b);
+              }
+            }
           }
         }
       }
@@ -145,6 +151,58 @@ __device__ __forceinline__ bool select_parallel(const uint32_t (&key)[kMaxExpert
   return true;
 }
 
+// Rank selection for E <= 64: each lane ranks its own (at most two) experts against all E
+// keys broadcast by shuffle, accumulating S_i = sum of p over experts ahead of it.  Under
+// the same exactness condition as select_parallel, S_i + p_i equals the sequential
+// cumulative sum at expert i's sorted position bit for bit; no sort and no scatter needed.
+template <int EPL>
+__device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPerLane], int E, float tau_b,
+                                            uint32_t& bits_out) {
+  const int lane = threadIdx.x & 31;
+  float S[EPL];
+  int rank[EPL];
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) { S[r] = 0.f; rank[r] = 0; }
+#pragma unroll
+  for (int r2 = 0; r2 < EPL; ++r2) {
+#pragma unroll 8
+    for (int src = 0; src < 32; ++src) {
+      const uint32_t kj = __shfl_sync(0xffffffffu, key[r2], src);
+      const float pj = __uint_as_float(kj & 0xFFFF0000u);
+#pragma unroll
+      for (int r = 0; r < EPL; ++r) {
+        const bool g = kj > key[r];
+        S[r] += g ? pj : 0.f;
+        rank[r] += g;
+      }
+    }
+  }
+  uint32_t keep_bits = 0;
+  int first_rej = 1 << 20;
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) {
+    if (lane + 32 * r < E) {
+      const float c = S[r] + __uint_as_float(key[r] & 0xFFFF0000u);
+      const bool keep = rank[r] == 0 || bf16r(c) < tau_b;
+      keep_bits |= (uint32_t)keep << r;
+      if (!keep) first_rej = min(first_rej, rank[r]);
+    }
+  }
+  const int J = __reduce_min_sync(0xffffffffu, first_rej);
+  uint32_t bad = 0;
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) {
+    if (lane + 32 * r < E) {
+      const float p = __uint_as_float(key[r] & 0xFFFF0000u);
+      if (rank[r] <= J && p != 0.f && p < 1.52587890625e-05f) bad = 1;  // 2^-16
+      if (S[r] + p >= 2.f) bad = 1;
+    }
+  }
+  if (__any_sync(0xffffffffu, bad)) return false;
+  bits_out = keep_bits;
+  return true;
+}
+
 // l[i] holds the bf16-valued logit of expert e = lane + 32*i (e < E).  On return w[i] is the
 // gate weight (0 when not selected) and the returned bitmask has bit i set when expert
 // lane + 32*i was selected.  Each probability is a bf16 value, so its fp32 bit pattern has
@@ -180,8 +238,8 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   }
   uint32_t bits = 0;
   bool done;
-  if (E <= 32) done = select_parallel<1>(key, E, tau_b, bits);
-  else if (E <= 64) done = select_parallel<2>(key, E, tau_b, bits);
+  if (E <= 32) done = select_rank<1>(key, E, tau_b, bits);
+  else if (E <= 64) done = select_rank<2>(key, E, tau_b, bits);
   else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
   else done = select_parallel<8>(key, E, tau_b, bits);
   if (!done) bits = select_sequential(key, E, tau_b);
