@@ -104,6 +104,22 @@ PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hi
                  void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
                  void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Fused decode that allocates nothing and takes no workspace: for callers that cannot call
+ * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts
+ * that only hand over inputs and outputs, latency-critical paths where an allocation would
+ * synchronise the device).  No counterpart in the reference.  Same kernel and results as
+ * ppmoe_decode without bias and side outputs; its scratch is a ~1 MiB array inside this
+ * library's device memory, held by every GPU that loads the library until process exit.
+ *   Limit: 1 <= tokens <= 16 and tokens * hidden <= 8192 (PPMOE_ERR_UNSUPPORTED beyond).
+ *   The first call on a device looks up the array's device address; make that first call
+ *   before any stream capture.  All calls share the one array: calls that can overlap on
+ *   the GPU (different streams, or different host threads) race and must be serialised by
+ *   the caller.  Each call clears the array's status word and counters before its launch.
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API int ppmoe_decode_noalloc(const void* x, int tokens, const void* packed, int hidden, int experts,
+                                   int group, float tau, void* out, void* stream);
+
 /* Diagnostics: when `buf` (device, >= 32 * 8 bytes per CTA of the decode grid) is non-NULL,
  * later ppmoe_decode launches record per-CTA phase timestamps (SM clock64) into it; NULL
  * switches recording off.  No counterpart in the reference (it has no tracing). */
