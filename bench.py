@@ -69,9 +69,10 @@ class Clocks:
         self.path = f"/tmp/ppmoe_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
+        self.t_start = time.time()
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -79,6 +80,9 @@ class Clocks:
 
     def __exit__(self, *a):
         if self.proc:
+            # keep sampling until at least ~3 samples cover the region
+            while time.time() - self.t_start < 0.35:
+                time.sleep(0.02)
             self.proc.terminate()
             self.proc.wait()
 
@@ -97,6 +101,12 @@ class Clocks:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]),
                 "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def decode_traffic():
+    """DRAM bytes per decode launch from the committed ncu capture (profiles/)."""
+    p = os.path.join(ROOT, "profiles", "decode_fused_bs1.json")
+    return json.load(open(p))["dram_bytes_per_launch"] if os.path.exists(p) else None
 
 
 def cpu_baseline(layers, xs, seconds=10.0):
@@ -226,6 +236,7 @@ def main():
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        time.sleep(0.3)  # sampler start-up
         with torch.cuda.stream(stream):
             e0.record(stream)
             for _ in range(args.steps):
@@ -288,7 +299,7 @@ def main():
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": None, "bytes_per_launch": step_bytes / args.layers,
+                         "traffic": decode_traffic(), "bytes_per_launch": step_bytes / args.layers,
                          "kernel": "decode_fused_kernel<1,1>"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": args.layers * H * 2,
