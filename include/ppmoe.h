@@ -66,7 +66,7 @@ PPMOE_API int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_dow
  * Workspace: scratch the kernels keep between calls (cross-cluster partial sums,
  * self-resetting arrival counters, the device status word).  Size it with
  * ppmoe_workspace_bytes for the largest token count the caller will pass and zero it once
- * with ppmoe_workspace_init.  One workspace must not be used by two calls that can run
+ * with ppmoe_workspace_init (which clears the whole buffer).  One workspace must not be used by two calls that can run
  * concurrently (different streams).
  * ------------------------------------------------------------------------------------- */
 PPMOE_API size_t ppmoe_workspace_bytes(int max_tokens, int hidden, int experts, int group);
@@ -103,6 +103,24 @@ PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hi
                  int group, float tau, const float* logit_bias, void* out, void* logits_out,
                  void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
                  void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Prefill, any token count: tcgen05 router GEMM + selection, device-side dispatch (per-expert
+ * counts, 128-row tiles, token permutation; no host synchronisation), tcgen05 grouped
+ * gate/up GEMM with the SwiGLU epilogue, tcgen05 down GEMM with an fp32 per-token combine,
+ * one bf16 rounding.  Replaces TauSparseMoE.forward_prefill (tl:532-604) and its kernels
+ * moe_router_kernel, moe_select_expert_kernel, moe_local/global_scan_kernel,
+ * moe_dispatch_kernel, moe_fused_expert_kernel (tl:40-328).
+ *   Needs group % 16 == 0 and group <= 128 in addition to the shapes above.
+ *   Workspace: ppmoe_prefill_workspace_bytes(tokens, ...) bytes, 1024-byte aligned, zeroed once
+ *   (e.g. with ppmoe_workspace_init over its full size); a workspace sized for N tokens serves
+ *   any call with <= N tokens.  Its status word is read by ppmoe_workspace_status.
+ *   Other arguments as for ppmoe_decode.
+ * ------------------------------------------------------------------------------------- */
+PPMOE_API size_t ppmoe_prefill_workspace_bytes(int tokens, int hidden, int experts, int group);
+PPMOE_API int ppmoe_prefill(const void* x, int tokens, const void* packed, int hidden, int experts, int group,
+                            float tau, const float* logit_bias, void* out, void* logits_out, void* weights_out,
+                            int64_t* counts, void* ws, size_t ws_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call

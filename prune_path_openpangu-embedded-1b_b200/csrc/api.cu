@@ -26,6 +26,9 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
 
 void decode_set_trace(void*);
+size_t prefill_workspace_bytes(long long, int, int, int);
+int prefill_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*, int64_t*,
+                   void*, size_t, cudaStream_t);
 
 // Workspace header: status word, decode arrival counters; then the decode cluster partials.
 constexpr size_t kWsHeader = 256;
@@ -95,7 +98,8 @@ int ppmoe_workspace_init(void* ws, size_t ws_bytes, void* stream) {
     set_error("ppmoe_workspace_init: workspace must be >= %zu bytes and 256-byte aligned", kWsHeader);
     return PPMOE_ERR_INVALID_ARG;
   }
-  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, kWsHeader, static_cast<cudaStream_t>(stream)));
+  // the whole workspace: prefill's fp32 accumulator must start at zero as well
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, ws_bytes, static_cast<cudaStream_t>(stream)));
   return PPMOE_OK;
 }
 
@@ -163,6 +167,36 @@ int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int 
                        counts, ws, ws_bytes, pdl, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<uint32_t*>(w8), reinterpret_cast<uint32_t*>(w8 + kWsCounters),
                        reinterpret_cast<float*>(w8 + kWsHeader), ws_bytes - kWsHeader);
+}
+
+size_t ppmoe_prefill_workspace_bytes(int tokens, int hidden, int experts, int group) {
+  if (check_shape("ppmoe_prefill_workspace_bytes", hidden, experts, group) || tokens < 1) return 0;
+  return prefill_workspace_bytes(tokens, hidden, experts, group);
+}
+
+int ppmoe_prefill(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
+                  const float* logit_bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
+                  void* ws, size_t ws_bytes, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_shape("ppmoe_prefill", hidden, experts, group)) return rc;
+  if (group % 16 != 0 || group > 128) {
+    set_error("ppmoe_prefill: group=%d must be a multiple of 16 and <= 128", group);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (tokens < 1) {
+    set_error("ppmoe_prefill: tokens=%d must be >= 1", tokens);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (!x || !packed || !out || !ws) {
+    set_error("ppmoe_prefill: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(packed, 1024) || !aligned(ws, 1024)) {
+    set_error("ppmoe_prefill: x/out must be 16-byte, packed and ws 1024-byte aligned");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return prefill_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, out, logits_out, weights_out,
+                        counts, ws, ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

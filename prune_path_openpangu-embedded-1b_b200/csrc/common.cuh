@@ -96,6 +96,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(a, parity)) return true;
     if (i > 4096) __nanosleep(32);
+    // once any wait of this launch has given up, stop waiting quickly everywhere else
+    if ((i & 1023u) == 1023u && status && *reinterpret_cast<volatile uint32_t*>(status)) return false;
   }
   if (status) atomicOr(status, DEVERR_TIMEOUT);
   return false;

@@ -1,0 +1,618 @@
+// Prefill (more than 16 tokens): tcgen05 grouped GEMMs with device-side dispatch.
+//
+// Replaces TauSparseMoE.forward_prefill (src/tl_kernel_optimized_Ultimate_PanGU.py:532-604):
+//   moe_router_kernel (tl:40-91)            -> router_gemm_kernel (tcgen05, M=128 tokens,
+//                                             N=E, K=H) + route_logits_kernel (select.cuh)
+//   torch.sort + moe_select_expert_kernel + scatter_ (tl:557-564)  -> route_logits_kernel
+//   moe_local_scan / moe_global_scan (tl:133-212) + .item() sync   -> count / scan kernels;
+//                                             the worst-case-sized workspace removes the host
+//                                             sync and the 512-tile-per-expert cap (tl:176)
+//   moe_dispatch_kernel (tl:217-266)        -> scatter_kernel (token order within expert)
+//   moe_fused_expert_kernel (tl:271-328)    -> gu_gemm_kernel (gathered token rows x the
+//                                             expert's interleaved gate/up rows, SwiGLU and
+//                                             gate weight in the epilogue -> a2 rows) +
+//                                             down_gemm_kernel (a2 x down_t, fp32 reduction
+//                                             into a per-token accumulator) + convert_kernel
+// Numerics follow the reference's bf16 rounding points; the per-token combine over experts
+// accumulates in fp32 and rounds once (the reference Triton kernel adds bf16 atomics).
+#include <mutex>
+#include "umma.cuh"
+
+namespace ppmoe {
+
+int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t);
+
+constexpr int kTileM = 128;
+constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
+
+struct PrefillWs {
+  size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, pair_token, pair_w,
+      a2, out_acc, status, total;
+  long long max_pairs, max_tiles;
+  int nblocks;
+};
+
+static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
+  PrefillWs w;
+  w.nblocks = (int)((N + 255) / 256);
+  w.max_pairs = ((N * E + 127LL * E) + 127) / 128 * 128;
+  w.max_tiles = w.max_pairs / 128;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 1024); return r; };
+  w.status = take(64);
+  // the fp32 accumulator comes first so its place does not depend on the token count: a
+  // workspace zeroed once and sized for N tokens then serves every call with <= N tokens
+  w.out_acc = take((size_t)N * H * 4);
+  w.logits = take((size_t)N * E * 2);
+  w.weights = take((size_t)N * E * 2);
+  w.blockcnt = take((size_t)w.nblocks * E * 4);
+  w.blockoff = take((size_t)w.nblocks * E * 4);
+  w.count = take((size_t)E * 4);
+  w.exp_off = take((size_t)E * 4);
+  w.ntiles = take(16);
+  w.tile_expert = take((size_t)w.max_tiles * 4);
+  w.tile_row0 = take((size_t)w.max_tiles * 4);
+  w.pair_token = take((size_t)w.max_pairs * 4);
+  w.pair_w = take((size_t)w.max_pairs * 4);
+  w.a2 = take((size_t)w.max_pairs * G * 2);
+  w.total = o;
+  return w;
+}
+
+// ======================================================================== router GEMM
+struct RouterArgs {
+  int N, E, EP, H;
+  const float* bias;
+  __nv_bfloat16* logits;
+  uint32_t* status;
+};
+
+constexpr int kRouterStages = 4;
+
+__global__ void __launch_bounds__(192, 1)
+router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapR,
+                   const RouterArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)a.EP * 128;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRouterStages * stage_bytes);
+  uint64_t* empty = full + kRouterStages;
+  uint64_t* tfull = empty + kRouterStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
+  const int KB = a.H / kBK;
+  const uint32_t ncols = a.EP <= 32 ? 32 : a.EP <= 64 ? 64 : a.EP <= 128 ? 128 : 256;
+  if (tid == 0) {
+    for (int s = 0; s < kRouterStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    mbar_init(tfull, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, ncols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int tile = blockIdx.x;
+
+  if (warp == 4 && lane == 0) {  // TMA producer
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % kRouterStages;
+      mbar_wait(&empty[s], ((kb / kRouterStages) & 1) ^ 1, a.status);
+      uint8_t* st = smem + s * stage_bytes;
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
+      tma_load_2d(st, &mapX, kb * kBK, tile * kTileM, &full[s]);
+      tma_load_2d(st + a_bytes, &mapR, kb * kBK, 0, &full[s]);
+    }
+  } else if (warp == 5 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = umma_idesc_bf16(kTileM, a.EP);
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % kRouterStages;
+      mbar_wait(&full[s], (kb / kRouterStages) & 1, a.status);
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * stage_bytes);
+      const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k) umma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+      umma_commit(&empty[s]);
+    }
+    umma_commit(tfull);
+  } else if (warp < 4) {  // epilogue: row = token
+    mbar_wait(tfull, 0, a.status);
+    tc_fence_after();
+    const int t = tile * kTileM + warp * 32 + lane;
+    for (int c0 = 0; c0 < a.EP; c0 += 32) {
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+      if (t < a.N) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int e = c0 + j;
+          if (e < a.E) {
+            float l = bf16r(v[j]);
+            if (a.bias) l = bf16r(l + a.bias[e]);
+            a.logits[(size_t)t * a.E + e] = __float2bfloat16_rn(l);
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, ncols);
+  }
+}
+
+// ======================================================================== dispatch
+__global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, int* __restrict__ blockcnt) {
+  __shared__ int hist[256];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int t = blockIdx.x * 256 + threadIdx.x;
+  if (t < N)
+    for (int e = 0; e < E; ++e)
+      if (__bfloat162float(w[(size_t)t * E + e]) > 0.f) atomicAdd(&hist[e], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) blockcnt[(size_t)blockIdx.x * E + e] = hist[e];
+}
+
+// One CTA: per-expert prefix over token blocks, 128-padded expert offsets, tile list,
+// padding rows, activation counts.
+__global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E, int* __restrict__ blockoff,
+                            int* __restrict__ count, int* __restrict__ exp_off, int* __restrict__ ntiles,
+                            int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ pair_token,
+                            float* __restrict__ pair_w, long long* __restrict__ act_counts) {
+  __shared__ int off_s[257];
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E) {
+    for (int b = 0; b < nblocks; ++b) {
+      const int c = blockcnt[(size_t)b * E + e];
+      blockoff[(size_t)b * E + e] = run;
+      run += c;
+    }
+    count[e] = run;
+    if (act_counts) act_counts[e] += run;
+  }
+  __syncthreads();
+  if (e == 0) {
+    int o = 0;
+    for (int q = 0; q < E; ++q) {
+      off_s[q] = o;
+      o += (count[q] + kTileM - 1) / kTileM * kTileM;
+    }
+    off_s[E] = o;
+    *ntiles = o / kTileM;
+  }
+  __syncthreads();
+  if (e < E) {
+    const int o = off_s[e];
+    exp_off[e] = o;
+    const int padded = off_s[e + 1] - o;
+    for (int i = 0; i < padded / kTileM; ++i) {
+      tile_expert[o / kTileM + i] = e;
+      tile_row0[o / kTileM + i] = o + i * kTileM;
+    }
+    for (int p = o + run; p < o + padded; ++p) { pair_token[p] = -1; pair_w[p] = 0.f; }
+  }
+}
+
+// Per token block: (token, expert) pairs in token order within each expert.
+__global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, const int* __restrict__ blockoff,
+                               const int* __restrict__ exp_off, int* __restrict__ pair_token,
+                               float* __restrict__ pair_w) {
+  __shared__ int wsum[8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x * 256 + tid;
+  for (int e = 0; e < E; ++e) {
+    const float wv = t < N ? __bfloat162float(w[(size_t)t * E + e]) : 0.f;
+    const bool f = wv > 0.f;
+    const uint32_t b = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) wsum[warp] = __popc(b);
+    __syncthreads();
+    int before = 0;
+    for (int q = 0; q < warp; ++q) before += wsum[q];
+    if (f) {
+      const int pos = exp_off[e] + blockoff[(size_t)blockIdx.x * E + e] + before + __popc(b & ((1u << lane) - 1u));
+      pair_token[pos] = t;
+      pair_w[pos] = wv;
+    }
+    __syncthreads();
+  }
+}
+
+// ======================================================================== gate/up GEMM
+struct GUArgs {
+  const __nv_bfloat16* x;
+  int H, G;
+  const int* tile_expert;
+  const int* tile_row0;
+  const int* ntiles;
+  const int* pair_token;
+  const float* pair_w;
+  __nv_bfloat16* a2;  // [pairs][G]
+  uint32_t* status;
+};
+
+constexpr int kGUStages = 4;
+constexpr int kGULag = 2;  // cp.async groups kept in flight per producer thread
+
+__global__ void __launch_bounds__(320, 1)
+gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NB = 2 * a.G;  // interleaved gate/up rows = MMA N
+  const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)NB * 128;
+  const uint32_t stage_bytes = a_bytes + b_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGUStages * stage_bytes);
+  uint64_t* empty = full + kGUStages;
+  uint64_t* tfull = empty + kGUStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int KB = a.H / kBK;
+  const int ntiles = *a.ntiles;
+  if (tid == 0) {
+    for (int s = 0; s < kGUStages; ++s) { mbar_init(&full[s], 129); mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
+    fence_mbar_init();
+  }
+  if (warp == 8) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 4 && warp < 8) {  // producers: one gathered token row each; B via TMA
+    const int pr = tid - 128;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int e = a.tile_expert[tile];
+      int tok = a.pair_token[a.tile_row0[tile] + pr];
+      if (tok < 0) tok = 0;  // padding row: any valid row (its gate weight is 0)
+      const __nv_bfloat16* src = a.x + (size_t)tok * a.H;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % kGUStages;
+        mbar_wait(&empty[s], ((it / kGUStages) & 1) ^ 1, a.status);
+        uint8_t* st = smem + s * stage_bytes;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16(st + sw128_offset(pr, c), src + kb * kBK + c * 8);
+        cp_async_commit();
+        if (pr == 0) {
+          mbar_arrive_expect_tx(&full[s], b_bytes);
+          tma_load_3d(st + a_bytes, &mapGU, kb * kBK, 0, e * a.G, &full[s]);
+        }
+        if (it >= kGULag) {
+          cp_async_wait<kGULag>();
+          fence_proxy_async();
+          mbar_arrive(&full[(it - kGULag) % kGUStages]);
+        }
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async();
+    for (int j = max(0, it - kGULag); j < it; ++j) mbar_arrive(&full[j % kGUStages]);
+  } else if (warp == 8 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
+    int it = 0, tl = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+      const int acc = tl & 1;
+      mbar_wait(&tempty[acc], ((tl >> 1) & 1) ^ 1, a.status);
+      tc_fence_after();
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % kGUStages;
+        mbar_wait(&full[s], (it / kGUStages) & 1, a.status);
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * stage_bytes);
+        const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k)
+          umma_bf16(tmem + acc * 256, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&tfull[acc]);
+    }
+  } else if (warp < 4) {  // epilogue: row r = pair; SwiGLU with the reference's rounding points
+    const int r = warp * 32 + lane;
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+      const int acc = tl & 1;
+      mbar_wait(&tfull[acc], (tl >> 1) & 1, a.status);
+      tc_fence_after();
+      const int p = a.tile_row0[tile] + r;
+      const float wg = a.pair_w[p];
+      __nv_bfloat16* orow = a.a2 + (size_t)p * a.G;
+      for (int c0 = 0; c0 < NB; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          float o2[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float gb = bf16r(v[2 * (j + q)]), ub = bf16r(v[2 * (j + q) + 1]);
+            const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+            o2[q] = bf16r(bf16r(sb * ub) * wg);
+          }
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(o2[0], o2[1]);
+          pk[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + c0 / 2);
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ======================================================================== down GEMM + combine
+struct DownArgs {
+  int H, G, NCW;
+  const int* tile_expert;
+  const int* tile_row0;
+  const int* ntiles;
+  const int* pair_token;
+  float* out_acc;  // [N][H] fp32, zero on entry
+  uint32_t* status;
+};
+
+constexpr int kDownStages = 2;
+
+__global__ void __launch_bounds__(192, 1)
+down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
+                 const DownArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KB2 = (a.G + kBK - 1) / kBK;  // 1 or 2 (G <= 128)
+  const uint32_t a_kb = kTileM * 128;             // one 64-wide k-block of A
+  const uint32_t b_kb = (uint32_t)a.NCW * 128;    // one 64-wide k-block of a B chunk
+  const uint32_t a_bytes = KB2 * a_kb, b_bytes = KB2 * b_kb;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + a_bytes;
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(sB + kDownStages * b_bytes);
+  uint64_t* bempty = bfull + kDownStages;
+  uint64_t* afull = bempty + kDownStages;
+  uint64_t* aempty = afull + 1;
+  uint64_t* tfull = aempty + 1;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  const int NCH = a.H / a.NCW;
+  const int ntiles = *a.ntiles;
+  if (tid == 0) {
+    for (int s = 0; s < kDownStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
+    mbar_init(afull, 1);
+    mbar_init(aempty, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4 && lane == 0) {  // TMA producer
+    int tl = 0, ch = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+      const int e = a.tile_expert[tile], row0 = a.tile_row0[tile];
+      mbar_wait(aempty, (tl & 1) ^ 1, a.status);
+      mbar_arrive_expect_tx(afull, a_bytes);
+      for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + kb * a_kb, &mapA2, kb * kBK, row0, afull);
+      for (int c = 0; c < NCH; ++c, ++ch) {
+        const int s = ch % kDownStages;
+        mbar_wait(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
+        mbar_arrive_expect_tx(&bfull[s], b_bytes);
+        for (int kb = 0; kb < KB2; ++kb)
+          tma_load_2d(sB + s * b_bytes + kb * b_kb, &mapD, kb * kBK, e * a.H + c * a.NCW, &bfull[s]);
+      }
+    }
+  } else if (warp == 5 && lane == 0) {  // MMA issuer
+    const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
+    int tl = 0, ch = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+      mbar_wait(afull, tl & 1, a.status);
+      tc_fence_after();
+      for (int c = 0; c < NCH; ++c, ++ch) {
+        const int s = ch % kDownStages, acc = ch & 1;
+        mbar_wait(&tempty[acc], ((ch >> 1) & 1) ^ 1, a.status);
+        mbar_wait(&bfull[s], (ch / kDownStages) & 1, a.status);
+        tc_fence_after();
+        for (int k16 = 0; k16 < a.G / 16; ++k16) {
+          const int kb = k16 >> 2, kk = k16 & 3;
+          const uint64_t ad = umma_desc_sw128(smem_u32(sA + kb * a_kb)) + 2 * kk;
+          const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * b_bytes + kb * b_kb)) + 2 * kk;
+          umma_bf16(tmem + acc * 256, ad, bd, idesc, k16 != 0);
+        }
+        umma_commit(&bempty[s]);
+        umma_commit(&tfull[acc]);
+      }
+      umma_commit(aempty);
+    }
+  } else if (warp < 4) {  // epilogue: fp32 reduction of each pair row into its token's row
+    const int r = warp * 32 + lane;
+    int ch = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int tok = a.pair_token[a.tile_row0[tile] + r];
+      for (int c = 0; c < NCH; ++c, ++ch) {
+        const int acc = ch & 1;
+        mbar_wait(&tfull[acc], (ch >> 1) & 1, a.status);
+        tc_fence_after();
+        float* dst = a.out_acc + (size_t)(tok < 0 ? 0 : tok) * a.H + c * a.NCW;
+        for (int c0 = 0; c0 < a.NCW; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
+          if (tok >= 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) red_add_v4(dst + c0 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// fp32 accumulator -> bf16 output (one rounding); leaves the accumulator zeroed for the next call
+__global__ void convert_kernel(float4* __restrict__ acc, uint2* __restrict__ out, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = acc[i];
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    out[i] = pk;
+  }
+}
+
+// ======================================================================== host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map of rank 2 or 3, 128-byte swizzle, zero fill out of bounds.
+static int make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                    const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return PPMOE_ERR_CUDA;
+  }
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides_bytes,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PPMOE_ERR_CUDA;
+  }
+  return PPMOE_OK;
+}
+
+size_t prefill_workspace_bytes(long long N, int H, int E, int G) { return prefill_ws_layout(N, H, E, G).total; }
+
+int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G, float tau, const float* bias,
+                   void* out, void* logits_out, void* weights_out, int64_t* counts, void* wsp, size_t ws_bytes,
+                   cudaStream_t st) {
+  const PrefillWs W = prefill_ws_layout(N, H, E, G);
+  if (ws_bytes < W.total) {
+    set_error("ppmoe_prefill: workspace %zu < %zu bytes needed for %d tokens", ws_bytes, W.total, N);
+    return PPMOE_ERR_WORKSPACE;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(wsp);
+  const PackedLayout PL = packed_layout(H, E, G);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws + W.status);
+  __nv_bfloat16* logits = logits_out ? static_cast<__nv_bfloat16*>(logits_out)
+                                     : reinterpret_cast<__nv_bfloat16*>(ws + W.logits);
+  __nv_bfloat16* weights = weights_out ? static_cast<__nv_bfloat16*>(weights_out)
+                                       : reinterpret_cast<__nv_bfloat16*>(ws + W.weights);
+  int dev = 0, nsm = 0, rc;
+  PPMOE_CHECK_CUDA(cudaGetDevice(&dev));
+  PPMOE_CHECK_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+
+  // ---- router GEMM + selection
+  const int EP = (E + 15) / 16 * 16;
+  CUtensorMap mX, mR, mGU, mA2, mD;
+  {
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)N}, s[1] = {(cuuint64_t)H * 2};
+    cuuint32_t b[2] = {kBK, kTileM};
+    if ((rc = make_map(&mX, x, 2, d, s, b))) return rc;
+  }
+  {
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)E}, s[1] = {(cuuint64_t)H * 2};
+    cuuint32_t b[2] = {kBK, (cuuint32_t)EP};
+    if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
+  }
+  {
+    cuuint64_t d[3] = {(cuuint64_t)H, 2, (cuuint64_t)E * G}, s[2] = {(cuuint64_t)H * 2, (cuuint64_t)H * 6};
+    cuuint32_t b[3] = {kBK, 2, (cuuint32_t)G};
+    if ((rc = make_map(&mGU, pk + PL.experts, 3, d, s, b))) return rc;
+  }
+  {
+    cuuint64_t d[2] = {(cuuint64_t)G, (cuuint64_t)W.max_pairs}, s[1] = {(cuuint64_t)G * 2};
+    cuuint32_t b[2] = {kBK, kTileM};
+    if ((rc = make_map(&mA2, ws + W.a2, 2, d, s, b))) return rc;
+  }
+  const int NCW = H % 256 == 0 ? 256 : H % 128 == 0 ? 128 : 64;
+  {
+    cuuint64_t d[2] = {(cuuint64_t)G, (cuuint64_t)E * H}, s[1] = {(cuuint64_t)G * 2};
+    cuuint32_t b[2] = {kBK, (cuuint32_t)NCW};
+    if ((rc = make_map(&mD, pk + PL.down_t, 2, d, s, b))) return rc;
+  }
+
+  RouterArgs ra{N, E, EP, H, bias, logits, status};
+  const size_t r_smem = 1024 + kRouterStages * (kTileM * 128 + (size_t)EP * 128) + 256;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
+  router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  if ((rc = route_logits_launch(logits, N, E, tau, nullptr, weights, nullptr, st))) return rc;
+
+  // ---- dispatch
+  int* blockcnt = reinterpret_cast<int*>(ws + W.blockcnt);
+  int* blockoff = reinterpret_cast<int*>(ws + W.blockoff);
+  int* count = reinterpret_cast<int*>(ws + W.count);
+  int* exp_off = reinterpret_cast<int*>(ws + W.exp_off);
+  int* ntiles = reinterpret_cast<int*>(ws + W.ntiles);
+  int* tile_expert = reinterpret_cast<int*>(ws + W.tile_expert);
+  int* tile_row0 = reinterpret_cast<int*>(ws + W.tile_row0);
+  int* pair_token = reinterpret_cast<int*>(ws + W.pair_token);
+  float* pair_w = reinterpret_cast<float*>(ws + W.pair_w);
+  count_kernel<<<W.nblocks, 256, 0, st>>>(weights, N, E, blockcnt);
+  scan_kernel<<<1, 256, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
+                                 pair_token, pair_w, reinterpret_cast<long long*>(counts));
+  scatter_kernel<<<W.nblocks, 256, 0, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+
+  // ---- experts
+  const int grid = (int)std::min<long long>(nsm, W.max_tiles);
+  GUArgs ga{static_cast<const __nv_bfloat16*>(x), H, G, tile_expert, tile_row0, ntiles, pair_token, pair_w,
+            reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status};
+  const size_t g_smem = 1024 + kGUStages * (kTileM * 128 + (size_t)2 * G * 128) + 256;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g_smem));
+  gu_gemm_kernel<<<grid, 320, g_smem, st>>>(mGU, ga);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  DownArgs da{H, G, NCW, tile_expert, tile_row0, ntiles, pair_token, reinterpret_cast<float*>(ws + W.out_acc), status};
+  const int KB2 = (G + kBK - 1) / kBK;
+  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW * 128 + 256;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
+  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, da);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  const long long n4 = (long long)N * H / 4;
+  convert_kernel<<<(int)std::min<long long>((n4 + 255) / 256, (long long)nsm * 16), 256, 0, st>>>(
+      reinterpret_cast<float4*>(ws + W.out_acc), static_cast<uint2*>(out), n4);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return PPMOE_OK;
+}
+
+}  // namespace ppmoe

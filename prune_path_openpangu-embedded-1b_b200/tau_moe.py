@@ -10,7 +10,7 @@ Mirrors the reference module ``TauSparseMoE``
   (src/openpangu_moe.py:239-243);
 * mutable attribute ``tau`` (src/openpangu_moe.py:226);
 * ``forward(x [B,L,H]) -> [B,L,H]`` bf16 (tl:606-615): up to 16 tokens go through the
-  fused single-launch decode kernel, more tokens through the prefill path.
+  fused single-launch decode kernel, more tokens through the tcgen05 prefill path.
 
 The packed layout the kernels read is derived on the device from those four buffers and
 rebuilt automatically whenever one of them is replaced or modified in place.  Every call is
@@ -56,7 +56,8 @@ class TauSparseMoE(nn.Module):
         self._packed_key = None
         self._ws = None
         self._ws_tokens = 0
-        self._prefill = None
+        self._pws = None
+        self._pws_tokens = 0
 
     # ------------------------------------------------------------------ packing
     def _weights_key(self):
@@ -99,9 +100,10 @@ class TauSparseMoE(nn.Module):
 
     def check_device_status(self) -> None:
         """Synchronise and raise if a kernel recorded a device-side error (bounded wait ran
-        out); clears the status word."""
-        if self._ws is not None:
-            _lib.call("ppmoe_workspace_status", self._ws.data_ptr(), _stream_handle(self._ws.device))
+        out); clears the status words."""
+        for ws in (self._ws, self._pws):
+            if ws is not None:
+                _lib.call("ppmoe_workspace_status", ws.data_ptr(), _stream_handle(ws.device))
 
     # ------------------------------------------------------------------ forward
     def forward_decode(self, x_flat: torch.Tensor, *, logits_out=None, weights_out=None,
@@ -119,11 +121,34 @@ class TauSparseMoE(nn.Module):
                   ws.data_ptr(), ws.numel(), int(pdl), _stream_handle(x_flat.device))
         return out
 
-    def forward_prefill(self, x_flat: torch.Tensor, **kw) -> torch.Tensor:
-        from . import prefill  # noqa: WPS433 (kept lazy: prefill owns large workspaces)
-        if self._prefill is None:
-            self._prefill = prefill.PrefillEngine(self)
-        return self._prefill(x_flat, **kw)
+    def prefill_workspace(self, tokens: int) -> torch.Tensor:
+        """Worst-case-sized prefill workspace (grown on demand, zeroed once)."""
+        dev = self.W_gate.device
+        if self._pws is None or self._pws_tokens < tokens or self._pws.device != dev:
+            n = _lib.load().ppmoe_prefill_workspace_bytes(tokens, self.hidden_size, self.num_experts,
+                                                          self.group_size)
+            if n == 0:
+                raise _lib.PPMoEError("ppmoe_prefill_workspace_bytes", -2, _lib.load().ppmoe_last_error().decode())
+            buf = torch.empty(n + 1024, dtype=torch.uint8, device=dev)
+            off = (-buf.data_ptr()) % 1024
+            ws = buf[off:off + n]
+            _lib.call("ppmoe_workspace_init", ws.data_ptr(), n, _stream_handle(dev))
+            self._pws, self._pws_tokens = ws, tokens
+        return self._pws
+
+    def forward_prefill(self, x_flat: torch.Tensor, *, logits_out=None, weights_out=None) -> torch.Tensor:
+        N, H = x_flat.shape
+        out = torch.empty(N, H, dtype=torch.bfloat16, device=x_flat.device)
+        ws = self.prefill_workspace(N)
+        bias = self.logit_bias
+        if bias is not None:
+            bias = bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
+        counts = self.activated_statistics if self.track_statistics else None
+        _lib.call("ppmoe_prefill", x_flat.data_ptr(), N, self.packed().data_ptr(), H, self.num_experts,
+                  self.group_size, float(self.tau), _lib.ptr(bias), out.data_ptr(), _lib.ptr(logits_out),
+                  _lib.ptr(weights_out), _lib.ptr(counts), ws.data_ptr(), ws.numel(),
+                  _stream_handle(x_flat.device))
+        return out
 
     def forward(self, x: torch.Tensor, **kw) -> torch.Tensor:
         B, L, H = x.shape
