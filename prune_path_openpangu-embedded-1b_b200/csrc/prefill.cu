@@ -367,6 +367,7 @@ struct DownArgs {
 };
 
 constexpr int kDownStages = 2;
+constexpr int kStgPitch = 68;  // floats per staged 64-column row (+16 B against bank conflicts)
 
 __global__ void __launch_bounds__(192, 1)
 down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
@@ -387,6 +388,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   uint64_t* tfull = aempty + 1;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 128));
   const int NCH = a.H / a.NCW;
   const int ntiles = *a.ntiles;
   if (tid == 0) {
@@ -440,8 +442,12 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
       umma_commit(aempty);
     }
   } else if (warp < 4) {  // epilogue: fp32 reduction of each pair row into its token's row
+    // Each thread stages 64 columns of its own row in shared memory and hands them to the TMA
+    // unit as one 256-byte bulk reduce-add into the token's fp32 accumulator row (double
+    // buffered per thread; no cross-thread synchronisation needed).
     const int r = warp * 32 + lane;
-    int ch = 0;
+    float* stage = reinterpret_cast<float*>(stg) + (size_t)r * (2 * kStgPitch);
+    int ch = 0, sub = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int tok = a.pair_token[a.tile_row0[tile] + r];
       for (int c = 0; c < NCH; ++c, ++ch) {
@@ -449,18 +455,28 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
         mbar_wait(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
         float* dst = a.out_acc + (size_t)(tok < 0 ? 0 : tok) * a.H + c * a.NCW;
-        for (int c0 = 0; c0 < a.NCW; c0 += 32) {
+        for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
+          float* buf = stage + (sub & 1) * kStgPitch;
+          bulk_wait_read<1>();  // the reduce that last read this buffer has consumed it
           float v[32];
-          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
-          if (tok >= 0) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) red_add_v4(dst + c0 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32 * h, v);
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(buf + 32 * h + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
           }
+          if (tok >= 0) {
+            fence_proxy_async();
+            bulk_reduce_add_f32(dst + c0, buf, 256);
+          }
+          bulk_commit();
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       }
     }
+    bulk_wait<0>();
   }
   __syncthreads();
   if (warp == 5) {
@@ -564,7 +580,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     cuuint32_t b[2] = {kBK, kTileM};
     if ((rc = make_map(&mA2, ws + W.a2, 2, d, s, b))) return rc;
   }
-  const int NCW = H % 256 == 0 ? 256 : H % 128 == 0 ? 128 : 64;
+  const int NCW = H % 128 == 0 ? 128 : 64;  // B chunk stages stay small beside the staging rows
   {
     cuuint64_t d[2] = {(cuuint64_t)G, (cuuint64_t)E * H}, s[1] = {(cuuint64_t)G * 2};
     cuuint32_t b[2] = {kBK, (cuuint32_t)NCW};
@@ -604,7 +620,9 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   PPMOE_CHECK_CUDA(cudaGetLastError());
   DownArgs da{H, G, NCW, tile_expert, tile_row0, ntiles, pair_token, reinterpret_cast<float*>(ws + W.out_acc), status};
   const int KB2 = (G + kBK - 1) / kBK;
-  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW * 128 + 256;
+  const int NCW_ = NCW;
+  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
+                        (size_t)kTileM * 2 * kStgPitch * 4 + 128;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
   down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());

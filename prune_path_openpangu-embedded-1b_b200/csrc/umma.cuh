@@ -112,3 +112,19 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 }
 
 }  // namespace ppmoe
+
+namespace ppmoe {
+// Bulk fp32 reduce-add of `bytes` contiguous bytes from this CTA's shared memory into global
+// memory, performed by the TMA unit (tracked in this thread's bulk async-group).
+__device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;"
+               ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {  // source smem of all but N groups reusable
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory"); }
+}  // namespace ppmoe
