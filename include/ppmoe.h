@@ -122,6 +122,22 @@ PPMOE_API int ppmoe_prefill(const void* x, int tokens, const void* packed, int h
                             float tau, const float* logit_bias, void* out, void* logits_out, void* weights_out,
                             int64_t* counts, void* ws, size_t ws_bytes, void* stream);
 
+/* Router half of ppmoe_prefill (router GEMM + selection): gate weights [N][E] bf16 (0 where
+ * unselected) into weights_out, bf16 logits into logits_out (optional).  Replaces
+ * moe_router_kernel + torch.sort + moe_select_expert_kernel + scatter_ (tl:40-124, 550-564).
+ * Used by expert-parallel prefill on each rank's token shard. */
+PPMOE_API int ppmoe_prefill_route(const void* x, int tokens, const void* packed, int hidden, int experts,
+                                  int group, float tau, const float* logit_bias, void* logits_out,
+                                  void* weights_out, void* ws, size_t ws_bytes, void* stream);
+/* Expert half of ppmoe_prefill for rows whose gate weights are given (weights [N][E] bf16,
+ * 0 = expert not selected): dispatch + grouped gate/up + down GEMMs; out_f32 [N][H] receives
+ * the fp32 sums over the given experts (no bf16 rounding, so partial sums from several
+ * expert shards can be added exactly as the single-device path would).  Replaces
+ * moe_local/global_scan, moe_dispatch and moe_fused_expert kernels (tl:133-328, 566-604). */
+PPMOE_API int ppmoe_prefill_experts(const void* x, int tokens, const void* packed, int hidden, int experts,
+                                    int group, const void* weights, float* out_f32, int64_t* counts, void* ws,
+                                    size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts

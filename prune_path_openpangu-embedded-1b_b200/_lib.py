@@ -36,6 +36,10 @@ SIGNATURES = {
                                     _c_void_p]),
     "ppmoe_debug_trace": (None, [_c_void_p]),
     "ppmoe_prefill_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
+    "ppmoe_prefill_route": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
+                                     _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
+    "ppmoe_prefill_experts": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p,
+                                       _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_prefill": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_decode_noalloc": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,

@@ -28,7 +28,7 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
 void decode_set_trace(void*);
 size_t prefill_workspace_bytes(long long, int, int, int);
 int prefill_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*, int64_t*,
-                   void*, size_t, cudaStream_t);
+                   void*, size_t, cudaStream_t, int);
 
 // Workspace header: status word, decode arrival counters; then the decode cluster partials.
 constexpr size_t kWsHeader = 256;
@@ -174,29 +174,59 @@ size_t ppmoe_prefill_workspace_bytes(int tokens, int hidden, int experts, int gr
   return prefill_workspace_bytes(tokens, hidden, experts, group);
 }
 
+static int prefill_checks(const char* fn, const void* x, int tokens, const void* packed, int hidden, int experts,
+                          int group, const void* out, const void* ws) {
+  if (int rc = check_shape(fn, hidden, experts, group)) return rc;
+  if (group % 16 != 0 || group > 128) {
+    set_error("%s: group=%d must be a multiple of 16 and <= 128", fn, group);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (tokens < 1) {
+    set_error("%s: tokens=%d must be >= 1", fn, tokens);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (!x || !packed || !out || !ws) {
+    set_error("%s: null pointer", fn);
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(packed, 1024) || !aligned(ws, 1024)) {
+    set_error("%s: x/out must be 16-byte, packed and ws 1024-byte aligned", fn);
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return PPMOE_OK;
+}
+
 int ppmoe_prefill(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
                   const float* logit_bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
                   void* ws, size_t ws_bytes, void* stream) {
   g_err[0] = 0;
-  if (int rc = check_shape("ppmoe_prefill", hidden, experts, group)) return rc;
-  if (group % 16 != 0 || group > 128) {
-    set_error("ppmoe_prefill: group=%d must be a multiple of 16 and <= 128", group);
-    return PPMOE_ERR_UNSUPPORTED;
-  }
-  if (tokens < 1) {
-    set_error("ppmoe_prefill: tokens=%d must be >= 1", tokens);
-    return PPMOE_ERR_UNSUPPORTED;
-  }
-  if (!x || !packed || !out || !ws) {
-    set_error("ppmoe_prefill: null pointer");
-    return PPMOE_ERR_INVALID_ARG;
-  }
-  if (!aligned(x, 16) || !aligned(out, 16) || !aligned(packed, 1024) || !aligned(ws, 1024)) {
-    set_error("ppmoe_prefill: x/out must be 16-byte, packed and ws 1024-byte aligned");
-    return PPMOE_ERR_INVALID_ARG;
-  }
+  if (int rc = prefill_checks("ppmoe_prefill", x, tokens, packed, hidden, experts, group, out, ws)) return rc;
   return prefill_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, out, logits_out, weights_out,
-                        counts, ws, ws_bytes, static_cast<cudaStream_t>(stream));
+                        counts, ws, ws_bytes, static_cast<cudaStream_t>(stream), 0);
+}
+
+int ppmoe_prefill_route(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
+                        const float* logit_bias, void* logits_out, void* weights_out, void* ws, size_t ws_bytes,
+                        void* stream) {
+  g_err[0] = 0;
+  if (int rc = prefill_checks("ppmoe_prefill_route", x, tokens, packed, hidden, experts, group, weights_out, ws))
+    return rc;
+  return prefill_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, weights_out, logits_out,
+                        weights_out, nullptr, ws, ws_bytes, static_cast<cudaStream_t>(stream), 1);
+}
+
+int ppmoe_prefill_experts(const void* x, int tokens, const void* packed, int hidden, int experts, int group,
+                          const void* weights, float* out_f32, int64_t* counts, void* ws, size_t ws_bytes,
+                          void* stream) {
+  g_err[0] = 0;
+  if (int rc = prefill_checks("ppmoe_prefill_experts", x, tokens, packed, hidden, experts, group, out_f32, ws))
+    return rc;
+  if (!weights) {
+    set_error("ppmoe_prefill_experts: null gate weights");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return prefill_launch(x, tokens, packed, hidden, experts, group, 0.f, nullptr, out_f32, nullptr,
+                        const_cast<void*>(weights), counts, ws, ws_bytes, static_cast<cudaStream_t>(stream), 2);
 }
 
 }  // extern "C"

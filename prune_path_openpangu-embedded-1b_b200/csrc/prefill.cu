@@ -498,6 +498,13 @@ __global__ void convert_kernel(float4* __restrict__ acc, uint2* __restrict__ out
   }
 }
 
+__global__ void convert_f32_kernel(float4* __restrict__ acc, float4* __restrict__ out, long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    out[i] = acc[i];
+    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 // ======================================================================== host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -537,9 +544,14 @@ static int make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t
 
 size_t prefill_workspace_bytes(long long N, int H, int E, int G) { return prefill_ws_layout(N, H, E, G).total; }
 
+// mode: kPrefillFull (router -> selection -> experts -> bf16 out), kPrefillRouteOnly (stop
+// after the gate weights), kPrefillExperts (gate weights given in weights_out; expert compute
+// only; `out` receives fp32 partial sums instead of bf16).
+enum { kPrefillFull = 0, kPrefillRouteOnly = 1, kPrefillExperts = 2 };
+
 int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G, float tau, const float* bias,
                    void* out, void* logits_out, void* weights_out, int64_t* counts, void* wsp, size_t ws_bytes,
-                   cudaStream_t st) {
+                   cudaStream_t st, int mode) {
   const PrefillWs W = prefill_ws_layout(N, H, E, G);
   if (ws_bytes < W.total) {
     set_error("ppmoe_prefill: workspace %zu < %zu bytes needed for %d tokens", ws_bytes, W.total, N);
@@ -587,12 +599,15 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     if ((rc = make_map(&mD, pk + PL.down_t, 2, d, s, b))) return rc;
   }
 
+  if (mode != kPrefillExperts) {
   RouterArgs ra{N, E, EP, H, bias, logits, status};
   const size_t r_smem = 1024 + kRouterStages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
   router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   if ((rc = route_logits_launch(logits, N, E, tau, nullptr, weights, nullptr, st))) return rc;
+  }
+  if (mode == kPrefillRouteOnly) return PPMOE_OK;
 
   // ---- dispatch
   int* blockcnt = reinterpret_cast<int*>(ws + W.blockcnt);
@@ -627,8 +642,11 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   const long long n4 = (long long)N * H / 4;
-  convert_kernel<<<(int)std::min<long long>((n4 + 255) / 256, (long long)nsm * 16), 256, 0, st>>>(
-      reinterpret_cast<float4*>(ws + W.out_acc), static_cast<uint2*>(out), n4);
+  const int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)nsm * 16);
+  if (mode == kPrefillExperts)
+    convert_f32_kernel<<<cgrid, 256, 0, st>>>(reinterpret_cast<float4*>(ws + W.out_acc), static_cast<float4*>(out), n4);
+  else
+    convert_kernel<<<cgrid, 256, 0, st>>>(reinterpret_cast<float4*>(ws + W.out_acc), static_cast<uint2*>(out), n4);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
 }

@@ -1,0 +1,115 @@
+"""Expert-parallel prefill host logic on CPU ranks (gloo, world size 2): dispatch plan, count
+and payload exchange, partial return, deterministic combine.  Kernels are replaced by CPU
+stand-ins built from the oracle; the GPU path is covered by tests/test_ep_gpu.py."""
+import datetime
+import os
+import sys
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from conftest import MAX_ABS, MEAN_REL, ROOT, oracle, pkg
+
+
+def _cpu_route(L, tau):
+    O = oracle()
+
+    def route(x):
+        w, _ = O.softmax_thresholding(O.router_logits(x, L.router_w), tau)
+        return w
+    return route
+
+
+def _cpu_experts(L):
+    masks = F.one_hot(L.experts_id, L.experts).t().to(torch.bfloat16)  # [E, I]
+
+    def experts(xr, wr, e0):
+        el = wr.shape[1]
+        inter = F.silu(F.linear(xr, L.gate_w)) * F.linear(xr, L.up_w)
+        nm = wr @ masks[e0:e0 + el]
+        return F.linear((inter * nm).float(), L.down_w.float())
+    return experts
+
+
+def _worker(rank, world, port, q, mode):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+        P = pkg()
+        from importlib import import_module
+        ep = import_module(P.__name__ + ".ep")
+        L = P.synth.make_layer(8, 128, 16, 32, router_scale=1.75)
+        x = P.synth.make_tokens(8, 96, 128)
+        shard = x[rank * 48:(rank + 1) * 48]
+        # with injected kernels the layer only needs its shapes (no device weights)
+        m = ep.ExpertParallelMoE.__new__(ep.ExpertParallelMoE)
+        m.group, m.world, m.rank = None, world, rank
+        m.H, m.E, m.G, m.tau, m.el = 128, 16, 32, 0.7, 16 // world
+        m.route_fn, m.expert_fn, m.full, m.local, m.last_stats = _cpu_route(L, 0.7), _cpu_experts(L), None, None, {}
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("injected failure before dispatch")
+        y = m(shard)
+        outs = [torch.empty_like(y) for _ in range(world)]
+        dist.all_gather(outs, y)
+        q.put((rank, "ok", torch.cat(outs) if rank == 0 else None))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        q.put((rank, "err", repr(e)[:200]))
+    finally:
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:  # noqa: BLE001
+                pass
+
+
+def _run(mode, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() % 2000)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, status, payload = q.get(timeout=120)
+        res[r] = (status, payload)
+    for p in procs:
+        p.join(timeout=60)
+    return res
+
+
+def test_ep_two_ranks_matches_oracle():
+    res = _run("ok")
+    assert res[0][0] == "ok" and res[1][0] == "ok", res
+    y = res[0][1]
+    P = pkg()
+    L = P.synth.make_layer(8, 128, 16, 32, router_scale=1.75)
+    x = P.synth.make_tokens(8, 96, 128)
+    ref = oracle().moe_mlp(x, L, 0.7).out
+    d = (y.float() - ref.float()).abs()
+    assert d.max() <= MAX_ABS and d.sum() / ref.float().abs().sum() <= MEAN_REL
+
+
+def test_ep_rank_failure_surfaces_as_error():
+    res = _run("fail")
+    assert res[1][0] == "err" and "injected" in res[1][1]
+    assert res[0][0] == "err"  # the surviving rank's collective fails instead of hanging
+
+
+def test_dispatch_plan_and_combine_single_process():
+    ep = __import__(pkg().__name__ + ".ep", fromlist=["x"])
+    w = torch.zeros(5, 8, dtype=torch.bfloat16)
+    w[0, 1] = 0.5; w[0, 6] = 0.25; w[2, 5] = 1.0; w[3, 0] = 0.75; w[4, 7] = 0.5; w[4, 4] = 0.5
+    tok, sw, cnt = ep.dispatch_plan(w, 2)
+    assert cnt.tolist() == [2, 3]
+    assert tok.tolist() == [0, 3, 0, 2, 4]
+    assert sw[0].tolist() == [0.0, 0.5, 0.0, 0.0] and sw[4].tolist() == [0.5, 0.0, 0.0, 0.5]
+    back = torch.arange(5 * 3, dtype=torch.float32).view(5, 3)
+    out = ep.combine_partials(back, tok, cnt.tolist(), 5)
+    assert out[0].float().tolist() == (back[0] + back[2]).tolist()
+    assert out[1].float().abs().sum() == 0
