@@ -126,6 +126,85 @@ def cpu_baseline(layers, xs, seconds=10.0):
                                       f"(H={H}, E={E}, G={G}, tau={TAU}), median"}
 
 
+def bench_prefill(P, dev, steps, warmup):
+    """Config 3: 8 x 2048 tokens through one layer (tau 0.70), inputs resident in HBM."""
+    H_, E_, G_, tau = 1536, 64, 96, 0.70
+    L = P.synth.make_layer(0, H_, E_, G_, router_scale=1.75)
+    m = P.TauSparseMoE(H_, E_ * G_, E_, G_, tau).to(dev)
+    P.physical_reorder_for_inference(m, L.gate_w, L.up_w, L.down_w, L.router_w, F.one_hot(L.experts_id, E_).t(), tau)
+    x = P.synth.make_tokens(1, 16384, H_).to(dev)
+    w = torch.empty(16384, E_, dtype=torch.bfloat16, device=dev)
+    m.forward_prefill(x, weights_out=w)
+    k = int((w > 0).sum())
+    for _ in range(max(3, warmup)):
+        m.forward_prefill(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        m.forward_prefill(x)
+    e1.record()
+    torch.cuda.synchronize()
+    m.check_device_status()
+    us = e0.elapsed_time(e1) * 1e3 / steps
+    flops = 2 * 442368 * k + 2 * 1536 * 64 * 16384
+    peak = peak_tflops()
+    return {"workload": "prefill 8x2048 tokens, tau 0.70 (config 3)", "value": 16384 / us * 1e6,
+            "unit": "tokens/s", "us_per_step": us, "steps": steps, "sum_k": k,
+            "roofline": {"bound": "tensor", "achieved": flops / us / 1e6, "peak": peak[0], "unit": "TFLOP/s",
+                         "frac": flops / us / 1e6 / peak[0], "peak_kind": peak[1]},
+            "l2": "each step writes/reads ~1 GB of dispatch scratch (> L2)"}
+
+
+def bench_ep(P, dev, world, rank, steps, warmup, dist):
+    """Config 5: 65536 tokens (Zipf(1.2) router prior, tau 0.70), experts sharded over the
+    ranks, tokens split evenly; NCCL all-to-all dispatch and combine."""
+    from importlib import import_module
+    ep = import_module(PKG + ".ep")
+    H_, E_, G_, tau, total = 1536, 64, 96, 0.70, 65536
+    L = P.synth.make_layer(0, H_, E_, G_, router_scale=1.75)
+    m = P.TauSparseMoE(H_, E_ * G_, E_, G_, tau).to(dev)
+    P.physical_reorder_for_inference(m, L.gate_w, L.up_w, L.down_w, L.router_w, F.one_hot(L.experts_id, E_).t(), tau)
+    bias = P.synth.zipf_bias(E_, 1.2).to(dev)
+    epm = ep.ExpertParallelMoE(m.W_gate, m.W_up, m.W_down, m.router, E_, G_, tau, logit_bias=bias)
+    n = total // world
+    x = P.synth.make_tokens(5, total, H_)[rank * n:(rank + 1) * n].to(dev)
+    for _ in range(max(3, warmup)):
+        epm(x)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        epm(x)
+    e1.record()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / steps
+    rows = float(epm.last_stats.get("recv_rows", 0))
+    if dist:
+        t = torch.tensor([ms, rows], device=dev)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        mn = t.clone()
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        ms, rows_max, rows_min = mx[0].item(), mx[1].item(), mn[1].item()
+    else:
+        rows_max = rows_min = rows
+    return {"workload": f"EP prefill {total} tokens, zipf 1.2, tau 0.70 (config 5), ep{world}",
+            "value": total / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "scaling": "strong", "recv_rows_max_over_min": rows_max / max(rows_min, 1.0)}
+
+
+def peak_tflops():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def run_reference(args, rank):
     """--impl reference: the reference algorithm's own CPU path (oracle restatement)."""
     if rank != 0:
@@ -164,6 +243,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--no-ep", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
 
@@ -284,6 +364,8 @@ def main():
         e2e_ms = t.item()
     e2e_us = e2e_ms * 1e3 / (e2e_steps * args.layers)
 
+    pre = bench_prefill(P, dev, max(3, args.steps // 4), args.warmup) if world == 1 else None
+    epres = bench_ep(P, dev, world, rank, max(3, args.steps // 4), args.warmup, dist) if not args.no_ep else None
     if rank == 0:
         cpu = cpu_baseline(base, xs_cpu[:8], args.cpu_seconds) if world == 1 else None
         line = {
@@ -306,6 +388,8 @@ def main():
                     "d2h_bytes_per_step": args.layers * H * 2,
                     "path": "TauSparseMoE.forward, eager, pinned host x/out"},
             "gpu_launches": args.steps * args.layers,
+            "prefill": pre,
+            "prefill_ep": epres,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
