@@ -71,7 +71,7 @@ __device__ __forceinline__ unsigned long long clk64() {
 
 // Shared-memory carve-out (byte offsets from a 1 KiB aligned base).
 struct DecSmem {
-  uint32_t bars, x, part, lg, w, tokmask, ulist, misc, a2, ring, total;
+  uint32_t bars, x, part, lg, w, tokmask, ulist, misc, kbuf, a2, ring, total;
 };
 
 __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
@@ -85,6 +85,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   s.tokmask = o; o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.ulist = o;   o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
+  s.kbuf = o;    o = (uint32_t)align_up(o + (size_t)kDecWarps * 64 * 4, 128);
   s.a2 = o;      o = (uint32_t)align_up(o + (size_t)64 * NT * 4, 1024);  // >= max(warps, slots)
   s.ring = o;    o += (uint32_t)slots * 3u * (uint32_t)H * 2u;
   s.total = o;
@@ -199,8 +200,24 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   __syncthreads();
   PPMOE_TRACE(4);
 
-  // ---- 2. selection, one warp per token
-  #pragma unroll 1
+  // ---- 2. selection: a single token with E <= 64 is selected by the whole CTA, otherwise
+  // one warp per token
+  if (NT == 1 && E <= 64) {
+    float w[kMaxExpertsPerLane];
+    const uint32_t bits =
+        select_one_token_cta<kDecWarps>(lg, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf));
+    if (warp == 0) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E) {
+          ws[e] = w[i];
+          tokmask[e] = (bits >> i) & 1u;
+        }
+      }
+    }
+  } else
+#pragma unroll 1
   for (int t = warp; t < N; t += kDecWarps) {
     float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
 #pragma unroll
@@ -208,7 +225,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       const int e = lane + 32 * i;
       l[i] = e < E ? lg[t * E + e] : -INFINITY;
     }
-    const uint32_t bits = select_experts_warp(l, E, a.tau_b, w);
+    if (t == 0) PPMOE_TRACE(12);
+    const uint32_t bits = select_experts_warp(l, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf) + warp * 64);
+    if (t == 0) PPMOE_TRACE(13);
 #pragma unroll
     for (int i = 0; i < kMaxExpertsPerLane; ++i) {
       const int e = lane + 32 * i;
@@ -337,11 +356,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       for (int q = 0; q < VQ; ++q) {
         const int v = lane + 32 * q;
         if (v < H / 8) {
-          const __nv_bfloat16* rowp[4] = {g0, g0 + H, g1, g1 + H};
           const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xr[q]);
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(rowp[r] + v * 8);
+            const __nv_bfloat16* rp = ((r & 2) ? g1 : g0) + ((r & 1) ? H : 0);  // g0 u0 g1 u1
+            const uint4 rv = *reinterpret_cast<const uint4*>(rp + v * 8);
             const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&rv);
 #pragma unroll
             for (int h2 = 0; h2 < 4; ++h2) {
@@ -361,7 +380,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         for (int r = 0; r < 4; ++r) d[r] += __shfl_xor_sync(0xffffffffu, d[r], o);
       if (lane < 2 && (lane == 0 || two)) {
         const int n = lane == 0 ? n0 : n1;
-        const float gb = bf16r(d[2 * lane]), ub = bf16r(d[2 * lane + 1]);
+        const float gb = bf16r(lane == 0 ? d[0] : d[2]), ub = bf16r(lane == 0 ? d[1] : d[3]);
         const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
         const float ab = bf16r(sb * ub);
         a2s[n] = bf16r(ab * ws[ulist[(i0 + n) / G]]);

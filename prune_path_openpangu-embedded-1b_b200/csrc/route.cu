@@ -9,6 +9,7 @@ namespace ppmoe {
 __global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, int N, int E, float tau_b,
                                     const float* __restrict__ bias, __nv_bfloat16* __restrict__ w_out,
                                     uint8_t* __restrict__ mask_out) {
+  __shared__ __align__(16) uint32_t kbuf[8][64];
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= N) return;
@@ -23,7 +24,7 @@ __global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, in
     }
     l[i] = v;
   }
-  const uint32_t bits = select_experts_warp(l, E, tau_b, w);
+  const uint32_t bits = select_experts_warp(l, E, tau_b, w, kbuf[threadIdx.x >> 5]);
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = lane + 32 * i;

@@ -152,37 +152,46 @@ __device__ __forceinline__ bool select_parallel(const uint32_t (&key)[kMaxExpert
 }
 
 // Rank selection for E <= 64: each lane ranks its own (at most two) experts against all E
-// keys broadcast by shuffle, accumulating S_i = sum of p over experts ahead of it.  Under
+// keys (read four at a time from a 64-word per-warp shared buffer `kbuf`), accumulating
+// S_i = sum of p over experts ahead of it.  Under
 // the same exactness condition as select_parallel, S_i + p_i equals the sequential
 // cumulative sum at expert i's sorted position bit for bit; no sort and no scatter needed.
 template <int EPL>
 __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPerLane], int E, float tau_b,
-                                            uint32_t& bits_out) {
+                                            uint32_t& bits_out, uint32_t* kbuf) {
   const int lane = threadIdx.x & 31;
-  float S[EPL];
+  // every key to shared memory (padding keys are 0), then 4 keys per broadcast load
+#pragma unroll
+  for (int r = 0; r < EPL; ++r) kbuf[lane + 32 * r] = key[r];
+  __syncwarp();
+  float S[EPL][2];
   int rank[EPL];
 #pragma unroll
-  for (int r = 0; r < EPL; ++r) { S[r] = 0.f; rank[r] = 0; }
+  for (int r = 0; r < EPL; ++r) { S[r][0] = S[r][1] = 0.f; rank[r] = 0; }
 #pragma unroll
-  for (int r2 = 0; r2 < EPL; ++r2) {
-#pragma unroll 8
-    for (int src = 0; src < 32; ++src) {
-      const uint32_t kj = __shfl_sync(0xffffffffu, key[r2], src);
-      const float pj = __uint_as_float(kj & 0xFFFF0000u);
+  for (int j4 = 0; j4 < 8 * EPL; ++j4) {
+    const uint4 kq = reinterpret_cast<const uint4*>(kbuf)[j4];
+    const uint32_t kk[4] = {kq.x, kq.y, kq.z, kq.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float pj = __uint_as_float(kk[q] & 0xFFFF0000u);
 #pragma unroll
       for (int r = 0; r < EPL; ++r) {
-        const bool g = kj > key[r];
-        S[r] += g ? pj : 0.f;
+        const bool g = kk[q] > key[r];
+        S[r][q & 1] += g ? pj : 0.f;
         rank[r] += g;
       }
     }
   }
+  __syncwarp();
   uint32_t keep_bits = 0;
   int first_rej = 1 << 20;
+  float Sr[EPL];
 #pragma unroll
   for (int r = 0; r < EPL; ++r) {
+    Sr[r] = S[r][0] + S[r][1];  // exact under the condition checked below
     if (lane + 32 * r < E) {
-      const float c = S[r] + __uint_as_float(key[r] & 0xFFFF0000u);
+      const float c = Sr[r] + __uint_as_float(key[r] & 0xFFFF0000u);
       const bool keep = rank[r] == 0 || bf16r(c) < tau_b;
       keep_bits |= (uint32_t)keep << r;
       if (!keep) first_rej = min(first_rej, rank[r]);
@@ -195,7 +204,7 @@ __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPer
     if (lane + 32 * r < E) {
       const float p = __uint_as_float(key[r] & 0xFFFF0000u);
       if (rank[r] <= J && p != 0.f && p < 1.52587890625e-05f) bad = 1;  // 2^-16
-      if (S[r] + p >= 2.f) bad = 1;
+      if (Sr[r] + p >= 2.f) bad = 1;
     }
   }
   if (__any_sync(0xffffffffu, bad)) return false;
@@ -203,13 +212,15 @@ __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPer
   return true;
 }
 
-// l[i] holds the bf16-valued logit of expert e = lane + 32*i (e < E).  On return w[i] is the
+// l[i] holds the bf16-valued logit of expert e = lane + 32*i (e < E).  kbuf: 64 words of
+// 16-byte aligned shared memory owned by the calling warp.  On return w[i] is the
 // gate weight (0 when not selected) and the returned bitmask has bit i set when expert
 // lane + 32*i was selected.  Each probability is a bf16 value, so its fp32 bit pattern has
 // 16 zero low bits; the 32-bit key (bf16 bits of p) << 16 | (0xFFFF - e) orders candidates
 // by p descending and then by expert index ascending.
 __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
-                                                        float tau_b, float (&w)[kMaxExpertsPerLane]) {
+                                                        float tau_b, float (&w)[kMaxExpertsPerLane],
+                                                        uint32_t* kbuf) {
   const int lane = threadIdx.x & 31;
   uint32_t mk = 0u;
 #pragma unroll
@@ -238,14 +249,117 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   }
   uint32_t bits = 0;
   bool done;
-  if (E <= 32) done = select_rank<1>(key, E, tau_b, bits);
-  else if (E <= 64) done = select_rank<2>(key, E, tau_b, bits);
+  if (E <= 32) done = select_rank<1>(key, E, tau_b, bits, kbuf);
+  else if (E <= 64) done = select_rank<2>(key, E, tau_b, bits, kbuf);
   else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
   else done = select_parallel<8>(key, E, tau_b, bits);
   if (!done) bits = select_sequential(key, E, tau_b);
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i)
     w[i] = (bits >> i) & 1u ? bf16r(__frcp_rn(1.f + expf(-l[i]))) : 0.f;
+  return bits;
+}
+
+// CTA-parallel selection of ONE token for E <= 64, used by the single-token decode: every
+// warp computes the softmax keys redundantly (identical code, identical results); warp w
+// ranks experts (w % 2) * 32 + lane against the experts of part w / 2 (NW / 2 parts), the
+// partial ranks and mass sums meet in shared memory, and warp 0 finishes.  Same exactness
+// condition and fallback as select_rank.  All NW warps of the CTA must call it.
+// scratch: 2 * (NW / 2) * 64 words of shared memory.  Returns the kept-expert bitmask of
+// slot i (expert lane + 32 i) in warp 0 (other warps: 0) and writes w (warp 0 only valid).
+template <int NW>
+__device__ __forceinline__ uint32_t select_one_token_cta(const float* lg, int E, float tau_b,
+                                                         float (&w)[kMaxExpertsPerLane], uint32_t* scratch) {
+  constexpr int NP = NW / 2;  // rank parts
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float l[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) l[r] = lane + 32 * r < E ? lg[lane + 32 * r] : -INFINITY;
+  uint32_t mk = 0u;
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+    if (lane + 32 * r < E) mk = max(mk, float_order_key(l[r]));
+  const float m = float_from_order_key(__reduce_max_sync(0xffffffffu, mk));
+  float ex[2], s = 0.f;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    ex[r] = lane + 32 * r < E ? expf(l[r] - m) : 0.f;
+    s += ex[r];
+  }
+  s = warp_sum(s);
+  const float rs = __frcp_rn(s);
+  uint32_t key[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int e = lane + 32 * r;
+    key[r] = e < E ? (__float_as_uint(bf16r(__fmul_rn(ex[r], rs))) & 0xFFFF0000u) | (0xFFFFu - (uint32_t)e) : 0u;
+  }
+  // ---- partial ranks: own expert i = h*32 + lane against experts of part p
+  int* prank = reinterpret_cast<int*>(scratch);           // [NP][64]
+  float* psum = reinterpret_cast<float*>(scratch) + NP * 64;  // [NP][64]
+  if (warp < 2 * NP) {
+    const int h = warp & 1, p = warp >> 1;
+    const uint32_t mine = h ? key[1] : key[0];
+    const int j0 = (64 * p) / NP, j1 = (64 * (p + 1)) / NP;
+    float S = 0.f;
+    int rk = 0;
+#pragma unroll 4
+    for (int j = j0; j < j1; ++j) {
+      const uint32_t kj = __shfl_sync(0xffffffffu, (j & 32) ? key[1] : key[0], j & 31);
+      const bool g = kj > mine;
+      S += g ? __uint_as_float(kj & 0xFFFF0000u) : 0.f;
+      rk += g;
+    }
+    prank[p * 64 + h * 32 + lane] = rk;
+    psum[p * 64 + h * 32 + lane] = S;
+  }
+  __syncthreads();
+  uint32_t bits = 0;
+  if (warp == 0) {
+    float Sr[2];
+    int rank[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      Sr[r] = 0.f;
+      rank[r] = 0;
+#pragma unroll
+      for (int p = 0; p < NP; ++p) {
+        Sr[r] += psum[p * 64 + r * 32 + lane];
+        rank[r] += prank[p * 64 + r * 32 + lane];
+      }
+    }
+    uint32_t keep_bits = 0;
+    int first_rej = 1 << 20;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (lane + 32 * r < E) {
+        const float c = Sr[r] + __uint_as_float(key[r] & 0xFFFF0000u);
+        const bool keep = rank[r] == 0 || bf16r(c) < tau_b;
+        keep_bits |= (uint32_t)keep << r;
+        if (!keep) first_rej = min(first_rej, rank[r]);
+      }
+    }
+    const int J = __reduce_min_sync(0xffffffffu, first_rej);
+    uint32_t bad = 0;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (lane + 32 * r < E) {
+        const float p = __uint_as_float(key[r] & 0xFFFF0000u);
+        if (rank[r] <= J && p != 0.f && p < 1.52587890625e-05f) bad = 1;  // 2^-16
+        if (Sr[r] + p >= 2.f) bad = 1;
+      }
+    }
+    if (__any_sync(0xffffffffu, bad)) {
+      uint32_t k8[kMaxExpertsPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxExpertsPerLane; ++i) k8[i] = i < 2 ? key[i] : 0u;
+      keep_bits = select_sequential(k8, E, tau_b);
+    }
+    bits = keep_bits;
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i)
+      w[i] = (i < 2 && ((bits >> i) & 1u)) ? bf16r(__frcp_rn(1.f + expf(-l[i & 1]))) : 0.f;
+  }
   return bits;
 }
 
