@@ -74,6 +74,13 @@ struct DecSmem {
   uint32_t bars, x, part, lg, w, tokmask, ulist, misc, kbuf, a2, ring, total;
 };
 
+// A neuron's gate, up and down rows are one contiguous record in its ring slot (one bulk copy);
+// slots are 6H + 32 bytes apart, so the gate rows of 4 consecutive neurons start in 4
+// different 16-byte bank groups and an 8-row tensor-core fragment load (4 neurons x gate/up)
+// costs 2 shared-memory wavefronts instead of 8.
+__host__ __device__ inline uint32_t dec_row_pitch(int H) { return 2u * (uint32_t)H; }
+__host__ __device__ inline uint32_t dec_slot_bytes(int H) { return 6u * (uint32_t)H + 32u; }
+
 __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   DecSmem s;
   uint32_t o = 0;
@@ -87,7 +94,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
   s.kbuf = o;    o = (uint32_t)align_up(o + (size_t)kDecWarps * 64 * 4, 128);
   s.a2 = o;      o = (uint32_t)align_up(o + (size_t)64 * NT * 4, 1024);  // >= max(warps, slots)
-  s.ring = o;    o += (uint32_t)slots * 3u * (uint32_t)H * 2u;
+  s.ring = o;    o += (uint32_t)slots * dec_slot_bytes(H);
   s.total = o;
   return s;
 }
@@ -115,7 +122,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   int* misc = reinterpret_cast<int*>(smem + L.misc);  // [0]=|U| [1]=is_last
   float* a2s = reinterpret_cast<float*>(smem + L.a2);
   uint8_t* ring = smem + L.ring;
-  const uint32_t rec_bytes = 3u * (uint32_t)H * 2u;
+  const uint32_t rec_bytes = 3u * (uint32_t)H * 2u;  // one neuron record in the packed blob
+  const uint32_t rowp = dec_row_pitch(H), slotb = dec_slot_bytes(H);
 
   PPMOE_TRACE(0);
   // ---- prologue: barriers; router slice prefetch (weights only: legal before the PDL wait)
@@ -253,13 +261,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     i0 = (int)((long long)W * blockIdx.x / gridDim.x);
     cnt = (int)((long long)W * (blockIdx.x + 1) / gridDim.x) - i0;
   };
-  auto issue_neuron = [&](int n) {  // one record into slot n % slots
+  auto issue_neuron = [&](int n) {  // neuron n's three rows into slot n % slots
     const int gi = i0 + n;
     const int u = gi / G, j = gi - u * G;
     const int sl = n % a.slots;
+    const __nv_bfloat16* src = a.experts + ((size_t)ulist[u] * G + j) * 3 * H;
     mbar_arrive_expect_tx(&bars[sl], rec_bytes);
-    bulk_g2s(ring + (size_t)sl * rec_bytes, a.experts + ((size_t)ulist[u] * G + j) * 3 * H, rec_bytes,
-             &bars[sl], pol);
+    bulk_g2s(ring + (size_t)sl * slotb, src, rec_bytes, &bars[sl], pol);
   };
   if (warp == 0) {
     int base = 0;
@@ -277,19 +285,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     // the router slice / scratch in the ring is dead: every warp passed the barrier above
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     const int win = min(cnt, a.slots);
-    #pragma unroll 1
-    for (int n = lane; n < win; n += 32) {
-      const int gi = i0 + n;
-      const int u = gi / G, j = gi - u * G;
-      if (n == 0 || j == 0) {
-        const int len = min(G - j, win - n);
-        mbar_arrive_expect_tx(&bars[n], (uint32_t)len * rec_bytes);
-        bulk_g2s(ring + (size_t)n * rec_bytes, a.experts + ((size_t)ulist[u] * G + j) * 3 * H,
-                 (uint32_t)len * rec_bytes, &bars[n], pol);
-      } else {
-        mbar_arrive(&bars[n]);
-      }
-    }
+    for (int n = lane; n < win; n += 32) issue_neuron(n);
   }
   // optional side outputs from the first CTA of the grid
   if (blockIdx.x == 0) {
@@ -320,15 +316,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[c][t][q] = 0.f;
 
-  // Wait for every run of the first window before any slot is refilled: a run's records are
-  // signalled on its head slot's barrier, which is re-armed once that slot is refilled.
+  // Wait for the whole first window (the single-token path computes on all of it at once).
   {
     const int win = min(cnt, a.slots);
-    #pragma unroll 1
-    for (int n = 0; n < win;) {
-      mbar_wait(&bars[n], 0u, a.status);
-      n += G - (i0 + n) % G;
-    }
+#pragma unroll 1
+    for (int n = 0; n < win; ++n) mbar_wait(&bars[n], 0u, a.status);
   }
   PPMOE_TRACE(7);
 
@@ -338,53 +330,61 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   bool fast = false;
   if constexpr (NT == 1) fast = cnt <= a.slots && H <= 2048;
   if (fast) {
-    constexpr int VQ = 8;  // H / 8 vectors per row, 32 lanes -> <= 8 per lane at H <= 2048
-    uint4 xr[VQ];
+    // gate/up GEMV on the tensor cores: rows (neuron n gate, neuron n up) of 8 neurons form a
+    // 16-row A tile (ldmatrix from the padded ring), the token is column 0 of an 8-column B
+    // tile; warps split the tiles and the K range, partial sums meet in shared memory.
+    const int T = (cnt + 7) >> 3;
+    const int KS = kDecWarps / T;
+    const int ksteps = H / 16;
+    float* pgu = reinterpret_cast<float*>(smem + L.kbuf);  // [KS][T*16] (reuses the selection buffer)
+    if (warp < T * KS) {
+      const int tile = warp % T, ks = warp / T;
+      const int k0 = (ksteps * ks) / KS, k1 = (ksteps * (ks + 1)) / KS;
+      const int r = lane & 15;
+      int nr = tile * 8 + (r >> 1);
+      if (nr >= cnt) nr = 0;  // padding rows read a valid row; results are ignored
+      const uint32_t arow = smem_u32(ring + (size_t)nr * slotb + (r & 1) * rowp) + (lane >> 4) * 16;
+      const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xs);
+      // Four k-steps per round: all fragment loads of the round are issued before its MMAs
+      // (the loads are not volatile, so they can be scheduled ahead), two accumulator chains.
+      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      auto mma = [&](float (&dc)[4], const uint32_t (&af)[4], uint32_t b0, uint32_t b1) {
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                     "{%0,%1,%2,%3};"
+                     : "+f"(dc[0]), "+f"(dc[1]), "+f"(dc[2]), "+f"(dc[3])
+                     : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b0), "r"(b1));
+      };
+      for (int kk = k0; kk < k1; kk += 4) {
+        uint32_t af[4][4], bf[4][2];
 #pragma unroll
-    for (int q = 0; q < VQ; ++q) {
-      const int v = lane + 32 * q;
-      xr[q] = v < H / 8 ? *reinterpret_cast<const uint4*>(xs + v * 8) : make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll 1
-    for (int n0 = warp; n0 < cnt; n0 += 2 * kDecWarps) {
-      const int n1 = n0 + kDecWarps;
-      const bool two = n1 < cnt;
-      const __nv_bfloat16* g0 = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)n0 * rec_bytes);
-      const __nv_bfloat16* g1 = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)(two ? n1 : n0) * rec_bytes);
-      float acc4[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // g0 u0 g1 u1
-#pragma unroll
-      for (int q = 0; q < VQ; ++q) {
-        const int v = lane + 32 * q;
-        if (v < H / 8) {
-          const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xr[q]);
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const __nv_bfloat16* rp = ((r & 2) ? g1 : g0) + ((r & 1) ? H : 0);  // g0 u0 g1 u1
-            const uint4 rv = *reinterpret_cast<const uint4*>(rp + v * 8);
-            const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&rv);
-#pragma unroll
-            for (int h2 = 0; h2 < 4; ++h2) {
-              const float2 xf = __bfloat1622float2(xp[h2]);
-              const float2 wf = __bfloat1622float2(wp[h2]);
-              acc4[r][h2 & 1] = fmaf(xf.y, wf.y, fmaf(xf.x, wf.x, acc4[r][h2 & 1]));
-            }
-          }
+        for (int q = 0; q < 4; ++q) {
+          const int k = min(kk + q, k1 - 1);
+          asm("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+              : "=r"(af[q][0]), "=r"(af[q][1]), "=r"(af[q][2]), "=r"(af[q][3]) : "r"(arow + k * 32));
+          bf[q][0] = lane < 4 ? x32[k * 8 + lane] : 0u;
+          bf[q][1] = lane < 4 ? x32[k * 8 + 4 + lane] : 0u;
         }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (kk + q < k1) mma(d[q & 1], af[q], bf[q][0], bf[q][1]);
       }
-      float d[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) d[r] = acc4[r][0] + acc4[r][1];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int r = 0; r < 4; ++r) d[r] += __shfl_xor_sync(0xffffffffu, d[r], o);
-      if (lane < 2 && (lane == 0 || two)) {
-        const int n = lane == 0 ? n0 : n1;
-        const float gb = bf16r(lane == 0 ? d[0] : d[2]), ub = bf16r(lane == 0 ? d[1] : d[3]);
-        const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
-        const float ab = bf16r(sb * ub);
-        a2s[n] = bf16r(ab * ws[ulist[(i0 + n) / G]]);
+      const float d0 = d[0][0] + d[1][0], d2 = d[0][2] + d[1][2];
+      if ((lane & 3) == 0) {  // column 0: rows lane/4 and lane/4 + 8
+        pgu[ks * T * 16 + tile * 16 + (lane >> 2)] = d0;
+        pgu[ks * T * 16 + tile * 16 + (lane >> 2) + 8] = d2;
       }
+    }
+    __syncthreads();
+    if (tid < cnt) {
+      const int n = tid, tile = n >> 3, rg = 2 * (n & 7);
+      float g = 0.f, u = 0.f;
+      for (int ks = 0; ks < KS; ++ks) {  // fixed order
+        g += pgu[ks * T * 16 + tile * 16 + rg];
+        u += pgu[ks * T * 16 + tile * 16 + rg + 1];
+      }
+      const float gb = bf16r(g), ub = bf16r(u);
+      const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+      a2s[n] = bf16r(bf16r(sb * ub) * ws[ulist[(i0 + n) / G]]);
     }
     __syncthreads();
 #pragma unroll
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
           for (int q = 0; q < 4; ++q) {
             const int m = min(m0 + q, cnt - 1);
             dv[q] = *reinterpret_cast<const uint2*>(
-                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)m * rec_bytes) + 2 * H + h4 * 4);
+                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)m * slotb + 2 * rowp) + h4 * 4);
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -428,8 +428,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       if (n >= a.slots) mbar_wait(&bars[s], (uint32_t)((n / a.slots) & 1), a.status);
       const int e = ulist[(i0 + n) / G];
       uint32_t tm = tokmask[e];
-      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * rec_bytes);
-      const __nv_bfloat16* up = gate + H;
+      const __nv_bfloat16* gate = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * slotb);
+      const __nv_bfloat16* up = reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)s * slotb + rowp);
       #pragma unroll 1
       while (tm) {
         const int t = __ffs(tm) - 1;
@@ -481,7 +481,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
           for (int q = 0; q < 4; ++q) {
             const int m = min(m0 + q, nb - 1);
             const __nv_bfloat16* down =
-                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)((b0 + m) % a.slots) * rec_bytes) + 2 * H;
+                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)((b0 + m) % a.slots) * slotb + 2 * rowp);
             dv[q] = *reinterpret_cast<const uint2*>(down + h4 * 4);
           }
 #pragma unroll
@@ -631,7 +631,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
     const size_t need_ring = align_up((size_t)(H / kCluster) * E * 2, 128) +
                              (size_t)max(1, kDecWarps / ((E / 2 + 31) / 32)) * NT * E * 4;
     const size_t red_ring = (size_t)NT * H * 4;
-    if ((size_t)slots * 3 * H * 2 < need_ring || (size_t)slots * 3 * H * 2 < red_ring ||
+    if ((size_t)slots * dec_slot_bytes(H) < need_ring || (size_t)slots * dec_slot_bytes(H) < red_ring ||
         L.total + 1024 > (uint32_t)max_optin || slots < 2) {
       set_error("ppmoe_decode: shared memory budget exceeded (H=%d E=%d tokens=%d)", H, E, tokens);
       return PPMOE_ERR_UNSUPPORTED;
