@@ -198,6 +198,28 @@ def bench_ep(P, dev, world, rank, steps, warmup, dist):
             "scaling": "strong", "recv_rows_max_over_min": rows_max / max(rows_min, 1.0)}
 
 
+def bench_decoder(P, dev):
+    """Config 4: 26-layer synthetic decoder, prompt 512 random ids, greedy 128 new tokens,
+    batch 1 and 16, tau 0.70; PrunePath MoE MLP vs the dense SwiGLU MLP it replaces."""
+    from importlib import import_module
+    D = import_module(PKG + ".decoder")
+    res = {"workload": "synthetic 26-layer decoder, prompt 512, greedy 128 tokens, tau 0.70 (config 4)",
+           "unit": "generated tokens/s (decode phase, CUDA graph per step)"}
+    for mlp in ("moe", "dense"):
+        dec = D.SyntheticDecoder(D.DecoderConfig(mlp=mlp), dev, seed=0, max_batch=16)
+        for B in (1, 16):
+            ids = torch.randint(0, 153600, (B, 512), generator=torch.Generator().manual_seed(B)).to(dev)
+            dec.generate(ids, 8)  # warm-up and graph capture for this batch
+            _, pre_ms, dec_ms = dec.generate(ids, 128)
+            res[f"{mlp}_bs{B}"] = {"decode_tokens_per_s": B * 127 / (dec_ms * 1e-3), "prefill_ms": pre_ms,
+                                   "decode_ms_per_step": dec_ms / 127}
+        del dec
+        torch.cuda.empty_cache()
+    for B in (1, 16):
+        res[f"moe_vs_dense_bs{B}"] = res[f"moe_bs{B}"]["decode_tokens_per_s"] / res[f"dense_bs{B}"]["decode_tokens_per_s"]
+    return res
+
+
 def peak_tflops():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -244,6 +266,7 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-ep", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
 
@@ -365,6 +388,7 @@ def main():
     e2e_us = e2e_ms * 1e3 / (e2e_steps * args.layers)
 
     pre = bench_prefill(P, dev, max(3, args.steps // 4), args.warmup) if world == 1 else None
+    decr = bench_decoder(P, dev) if world == 1 and not args.no_decoder else None
     epres = bench_ep(P, dev, world, rank, max(3, args.steps // 4), args.warmup, dist) if not args.no_ep else None
     if rank == 0:
         cpu = cpu_baseline(base, xs_cpu[:8], args.cpu_seconds) if world == 1 else None
@@ -390,6 +414,7 @@ def main():
             "gpu_launches": args.steps * args.layers,
             "prefill": pre,
             "prefill_ep": epres,
+            "decoder": decr,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
