@@ -14,7 +14,6 @@ hot path this library rebuilds.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
 import torch
@@ -123,9 +122,11 @@ class SyntheticDecoder:
     def prefill(self, ids):
         cfg = self.cfg
         B, T = ids.shape
-        self.kv = [(torch.zeros(B, cfg.heads, cfg.max_seq, cfg.head_dim, dtype=torch.bfloat16, device=self.dev),
-                    torch.zeros(B, cfg.heads, cfg.max_seq, cfg.head_dim, dtype=torch.bfloat16, device=self.dev))
-                   for _ in range(cfg.layers)]
+        if self.kv is None or self.kv[0][0].shape[0] != B:  # persistent: captured graphs read them
+            self.kv = [(torch.zeros(B, cfg.heads, cfg.max_seq, cfg.head_dim, dtype=torch.bfloat16, device=self.dev),
+                        torch.zeros(B, cfg.heads, cfg.max_seq, cfg.head_dim, dtype=torch.bfloat16, device=self.dev))
+                       for _ in range(cfg.layers)]
+            self.graph = None
         x = self.embed[ids]
         pos = torch.arange(T, device=self.dev)
         for i, L in enumerate(self.layers):
@@ -143,13 +144,21 @@ class SyntheticDecoder:
     def generate(self, ids, new_tokens: int, use_graph: bool = True):
         """Greedy decode; returns (tokens [B, new_tokens], prefill_ms, decode_ms)."""
         B, T = ids.shape
+        if T + new_tokens > self.cfg.max_seq:
+            raise ValueError(f"prompt {T} + {new_tokens} new tokens exceed max_seq {self.cfg.max_seq}")
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         tok = self.prefill(ids)
         e1.record()
         out = [tok]
-        self._pos = torch.tensor([T], device=self.dev)
-        self._tok = tok.clone()
+        if use_graph and (self.graph is None or self._gB != B):
+            self._pos = torch.zeros(1, dtype=torch.long, device=self.dev)  # graph inputs: fixed tensors
+            self._tok = torch.zeros(B, dtype=torch.long, device=self.dev)
+        elif not use_graph:
+            self._pos = torch.zeros(1, dtype=torch.long, device=self.dev)
+            self._tok = torch.zeros(B, dtype=torch.long, device=self.dev)
+        self._pos.fill_(T)
+        self._tok.copy_(tok)
         if use_graph:
             if self.graph is None or self._gB != B:
                 s = torch.cuda.Stream(self.dev)

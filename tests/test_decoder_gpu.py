@@ -23,6 +23,7 @@ def test_graph_decode_matches_eager(cuda, mlp, batch):
     d = _dec(mlp, cuda)
     ids = torch.randint(0, 1000, (batch, 20), generator=torch.Generator().manual_seed(1)).to(cuda)
     t_graph, _, _ = d.generate(ids, 12, use_graph=True)
+    t_graph2, _, _ = d.generate(ids, 12, use_graph=True)  # replays the captured graph
     t_eager, _, _ = d.generate(ids, 12, use_graph=False)
-    assert torch.equal(t_graph, t_eager)
+    assert torch.equal(t_graph, t_eager) and torch.equal(t_graph2, t_eager)
     assert t_graph.shape == (batch, 12)
