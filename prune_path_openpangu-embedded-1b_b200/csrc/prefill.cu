@@ -61,13 +61,13 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
 
 // ======================================================================== router GEMM
 struct RouterArgs {
-  int N, E, EP, H;
+  int N, E, EP, H, stages;
   const float* bias;
   __nv_bfloat16* logits;
   uint32_t* status;
 };
 
-constexpr int kRouterStages = 4;
+
 
 __global__ void __launch_bounds__(192, 1)
 router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_constant__ CUtensorMap mapR,
@@ -77,14 +77,14 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)a.EP * 128;
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kRouterStages * stage_bytes);
-  uint64_t* empty = full + kRouterStages;
-  uint64_t* tfull = empty + kRouterStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.stages * stage_bytes);
+  uint64_t* empty = full + a.stages;
+  uint64_t* tfull = empty + a.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull + 1);
   const int KB = a.H / kBK;
   const uint32_t ncols = a.EP <= 32 ? 32 : a.EP <= 64 ? 64 : a.EP <= 128 ? 128 : 256;
   if (tid == 0) {
-    for (int s = 0; s < kRouterStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < a.stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     mbar_init(tfull, 1);
     fence_mbar_init();
   }
@@ -97,8 +97,8 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
 
   if (warp == 4 && lane == 0) {  // TMA producer
     for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kRouterStages;
-      mbar_wait(&empty[s], ((kb / kRouterStages) & 1) ^ 1, a.status);
+      const int s = kb % a.stages;
+      mbar_wait(&empty[s], ((kb / a.stages) & 1) ^ 1, a.status);
       uint8_t* st = smem + s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_2d(st, &mapX, kb * kBK, tile * kTileM, &full[s]);
@@ -107,8 +107,8 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
   } else if (warp == 5 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.EP);
     for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % kRouterStages;
-      mbar_wait(&full[s], (kb / kRouterStages) & 1, a.status);
+      const int s = kb % a.stages;
+      mbar_wait(&full[s], (kb / a.stages) & 1, a.status);
       tc_fence_after();
       const uint32_t sa = smem_u32(smem + s * stage_bytes);
       const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
@@ -147,15 +147,27 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
 
 // ======================================================================== dispatch
 __global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, int* __restrict__ blockcnt) {
-  __shared__ int hist[256];
-  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  // stage the block's 256 consecutive gate-weight rows (coalesced), then warp w counts
+  // experts w, w + 8, ... with one ballot per 32-token chunk
+  extern __shared__ __align__(16) uint8_t cn_smem[];
+  const int P = E + 2;
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(cn_smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(w + (size_t)t0 * E);
+  for (int i = tid; i < nt * E / 2; i += 256) {
+    const int r = (2 * i) / E, c = (2 * i) % E;
+    *reinterpret_cast<uint32_t*>(ws + r * P + c) = src[i];
+  }
   __syncthreads();
-  const int t = blockIdx.x * 256 + threadIdx.x;
-  if (t < N)
-    for (int e = 0; e < E; ++e)
-      if (__bfloat162float(w[(size_t)t * E + e]) > 0.f) atomicAdd(&hist[e], 1);
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) blockcnt[(size_t)blockIdx.x * E + e] = hist[e];
+  for (int e = warp; e < E; e += 8) {
+    int n = 0;
+    for (int c = 0; c < 8; ++c) {
+      const int r = c * 32 + lane;
+      n += __popc(__ballot_sync(0xffffffffu, r < nt && __bfloat162float(ws[r * P + e]) > 0.f));
+    }
+    if (lane == 0) blockcnt[(size_t)blockIdx.x * E + e] = n;
+  }
 }
 
 // One CTA: per-expert prefix over token blocks, 128-padded expert offsets, tile list,
@@ -165,15 +177,23 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
                             int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ pair_token,
                             float* __restrict__ pair_w, long long* __restrict__ act_counts) {
   __shared__ int off_s[257];
+  __shared__ int cnt_s[256];
   const int e = threadIdx.x;
   int run = 0;
   if (e < E) {
-    for (int b = 0; b < nblocks; ++b) {
-      const int c = blockcnt[(size_t)b * E + e];
-      blockoff[(size_t)b * E + e] = run;
-      run += c;
+    for (int b0 = 0; b0 < nblocks; b0 += 8) {  // eight independent loads in flight
+      int c[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) c[q] = b0 + q < nblocks ? blockcnt[(size_t)(b0 + q) * E + e] : 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (b0 + q < nblocks) {
+          blockoff[(size_t)(b0 + q) * E + e] = run;
+          run += c[q];
+        }
     }
     count[e] = run;
+    cnt_s[e] = run;
     if (act_counts) act_counts[e] += run;
   }
   __syncthreads();
@@ -181,7 +201,7 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
     int o = 0;
     for (int q = 0; q < E; ++q) {
       off_s[q] = o;
-      o += (count[q] + kTileM - 1) / kTileM * kTileM;
+      o += (cnt_s[q] + kTileM - 1) / kTileM * kTileM;
     }
     off_s[E] = o;
     *ntiles = o / kTileM;
@@ -203,23 +223,33 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
 __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, const int* __restrict__ blockoff,
                                const int* __restrict__ exp_off, int* __restrict__ pair_token,
                                float* __restrict__ pair_w) {
-  __shared__ int wsum[8];
+  // The block's 256 gate-weight rows are consecutive in memory: one coalesced copy into shared
+  // memory (row pitch E + 2 elements against bank conflicts).  Warp w owns experts w, w + 8, ...
+  // and walks the 8 token chunks in order, so each pair's slot is a running ballot prefix.
+  extern __shared__ __align__(16) uint8_t sc_smem[];
+  const int P = E + 2;
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(sc_smem);  // [256][E + 2]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t = blockIdx.x * 256 + tid;
-  for (int e = 0; e < E; ++e) {
-    const float wv = t < N ? __bfloat162float(w[(size_t)t * E + e]) : 0.f;
-    const bool f = wv > 0.f;
-    const uint32_t b = __ballot_sync(0xffffffffu, f);
-    if (lane == 0) wsum[warp] = __popc(b);
-    __syncthreads();
-    int before = 0;
-    for (int q = 0; q < warp; ++q) before += wsum[q];
-    if (f) {
-      const int pos = exp_off[e] + blockoff[(size_t)blockIdx.x * E + e] + before + __popc(b & ((1u << lane) - 1u));
-      pair_token[pos] = t;
-      pair_w[pos] = wv;
+  const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(w + (size_t)t0 * E);
+  for (int i = tid; i < nt * E / 2; i += 256) {
+    const int r = (2 * i) / E, c = (2 * i) % E;
+    *reinterpret_cast<uint32_t*>(ws + r * P + c) = src[i];
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += 8) {
+    int run = exp_off[e] + blockoff[(size_t)blockIdx.x * E + e];
+    for (int c = 0; c < 8; ++c) {
+      const int r = c * 32 + lane;
+      const float wv = r < nt ? __bfloat162float(ws[r * P + e]) : 0.f;
+      const uint32_t b = __ballot_sync(0xffffffffu, wv > 0.f);
+      if (wv > 0.f) {
+        const int pos = run + __popc(b & ((1u << lane) - 1u));
+        pair_token[pos] = t0 + r;
+        pair_w[pos] = wv;
+      }
+      run += __popc(b);
     }
-    __syncthreads();
   }
 }
 
@@ -271,14 +301,17 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int e = a.tile_expert[tile];
       int tok = a.pair_token[a.tile_row0[tile] + pr];
-      if (tok < 0) tok = 0;  // padding row: any valid row (its gate weight is 0)
-      const __nv_bfloat16* src = a.x + (size_t)tok * a.H;
+      // padding rows load nothing: their stale shared-memory contents only reach their own
+      // (discarded) accumulator rows, and skipping them avoids every CTA hammering one row
+      const bool real = tok >= 0;
+      const __nv_bfloat16* src = a.x + (size_t)(real ? tok : 0) * a.H;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % kGUStages;
         mbar_wait(&empty[s], ((it / kGUStages) & 1) ^ 1, a.status);
         uint8_t* st = smem + s * stage_bytes;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(st + sw128_offset(pr, c), src + kb * kBK + c * 8);
+        for (int c = 0; c < 8; ++c)
+          if (real) cp_async16(st + sw128_offset(pr, c), src + kb * kBK + c * 8);
         cp_async_commit();
         if (pr == 0) {
           mbar_arrive_expect_tx(&full[s], b_bytes);
@@ -600,8 +633,9 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   }
 
   if (mode != kPrefillExperts) {
-  RouterArgs ra{N, E, EP, H, bias, logits, status};
-  const size_t r_smem = 1024 + kRouterStages * (kTileM * 128 + (size_t)EP * 128) + 256;
+  const int rstages = EP <= 128 ? 6 : 4;  // stages in flight, within the shared-memory budget
+  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+  const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
   router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
   PPMOE_CHECK_CUDA(cudaGetLastError());
@@ -619,10 +653,13 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   int* tile_row0 = reinterpret_cast<int*>(ws + W.tile_row0);
   int* pair_token = reinterpret_cast<int*>(ws + W.pair_token);
   float* pair_w = reinterpret_cast<float*>(ws + W.pair_w);
-  count_kernel<<<W.nblocks, 256, 0, st>>>(weights, N, E, blockcnt);
+  const size_t sc_smem = (size_t)256 * (E + 2) * 2;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
+  count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, N, E, blockcnt);
   scan_kernel<<<1, 256, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
                                  pair_token, pair_w, reinterpret_cast<long long*>(counts));
-  scatter_kernel<<<W.nblocks, 256, 0, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w);
+  scatter_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w);
   PPMOE_CHECK_CUDA(cudaGetLastError());
 
   // ---- experts
