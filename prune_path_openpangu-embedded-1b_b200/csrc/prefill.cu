@@ -215,8 +215,10 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
       tile_expert[o / kTileM + i] = e;
       tile_row0[o / kTileM + i] = o + i * kTileM;
     }
-    for (int p = o + run; p < o + padded; ++p) { pair_token[p] = -1; pair_w[p] = 0.f; }
   }
+  // padding rows of every expert's last tile, spread over the whole block
+  for (int q = 0; q < E; ++q)
+    for (int p = off_s[q] + cnt_s[q] + e; p < off_s[q + 1]; p += blockDim.x) { pair_token[p] = -1; pair_w[p] = 0.f; }
 }
 
 // Per token block: (token, expert) pairs in token order within each expert.
