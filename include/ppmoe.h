@@ -138,6 +138,14 @@ PPMOE_API int ppmoe_prefill_experts(const void* x, int tokens, const void* packe
                                     int group, const void* weights, float* out_f32, int64_t* counts, void* ws,
                                     size_t ws_bytes, void* stream);
 
+/* Expert-parallel prefill, source side: out[t] = bf16( sum over d = 0..ranks-1 of
+ * back[row_of[d][t]] ) with fp32 additions in rank order, skipping row_of = -1.
+ * back [rows][hidden] fp32 (the partial sums returned by the expert-owning ranks), row_of
+ * [ranks][tokens] int32, out [tokens][hidden] bf16; ranks <= 8.  No reference counterpart
+ * (the reference runs on one device). */
+PPMOE_API int ppmoe_ep_combine(const float* back, const int32_t* row_of, int ranks, int tokens, int hidden,
+                               void* out, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts

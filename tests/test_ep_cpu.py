@@ -26,10 +26,9 @@ def _cpu_route(L, tau):
 def _cpu_experts(L):
     masks = F.one_hot(L.experts_id, L.experts).t().to(torch.bfloat16)  # [E, I]
 
-    def experts(xr, wr, e0):
-        el = wr.shape[1]
+    def experts(xr, wr, own):
         inter = F.silu(F.linear(xr, L.gate_w)) * F.linear(xr, L.up_w)
-        nm = wr @ masks[e0:e0 + el]
+        nm = wr @ masks[own]
         return F.linear((inter * nm).float(), L.down_w.float())
     return experts
 
@@ -106,10 +105,14 @@ def test_dispatch_plan_and_combine_single_process():
     w = torch.zeros(5, 8, dtype=torch.bfloat16)
     w[0, 1] = 0.5; w[0, 6] = 0.25; w[2, 5] = 1.0; w[3, 0] = 0.75; w[4, 7] = 0.5; w[4, 4] = 0.5
     tok, sw, cnt = ep.dispatch_plan(w, 2)
-    assert cnt.tolist() == [2, 3]
-    assert tok.tolist() == [0, 3, 0, 2, 4]
-    assert sw[0].tolist() == [0.0, 0.5, 0.0, 0.0] and sw[4].tolist() == [0.5, 0.0, 0.0, 0.5]
-    back = torch.arange(5 * 3, dtype=torch.float32).view(5, 3)
+    # rank 0 owns experts 0,2,4,6; rank 1 owns 1,3,5,7
+    assert cnt.tolist() == [3, 3]
+    assert tok.tolist() == [0, 3, 4, 0, 2, 4]
+    assert sw[0].tolist() == [0.0, 0.0, 0.0, 0.25] and sw[1].tolist() == [0.75, 0.0, 0.0, 0.0]
+    assert sw[2].tolist() == [0.0, 0.0, 0.5, 0.0] and sw[3].tolist() == [0.5, 0.0, 0.0, 0.0]
+    assert sw[4].tolist() == [0.0, 0.0, 1.0, 0.0] and sw[5].tolist() == [0.0, 0.0, 0.0, 0.5]
+    back = torch.arange(6 * 3, dtype=torch.float32).view(6, 3)
     out = ep.combine_partials(back, tok, cnt.tolist(), 5)
-    assert out[0].float().tolist() == (back[0] + back[2]).tolist()
+    assert out[0].float().tolist() == (back[0] + back[3]).tolist()
+    assert out[4].float().tolist() == (back[2] + back[5]).tolist()
     assert out[1].float().abs().sum() == 0
