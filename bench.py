@@ -267,6 +267,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--no-ep", action="store_true")
     ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--profile-prefill", type=int, default=0,
+                    help="only run 3 prefill calls of this many tokens (for ncu captures) and exit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
 
@@ -275,6 +277,19 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile_prefill:
+        P = importlib.import_module(PKG)
+        dev = torch.device("cuda", local)
+        L = P.synth.make_layer(0, H, E, G, router_scale=1.75)
+        m = P.TauSparseMoE(H, E * G, E, G, 0.70).to(dev)
+        P.physical_reorder_for_inference(m, L.gate_w, L.up_w, L.down_w, L.router_w,
+                                         F.one_hot(L.experts_id, E).t(), 0.70)
+        x = P.synth.make_tokens(1, args.profile_prefill, H).to(dev)
+        for _ in range(3):
+            m.forward_prefill(x)
+        torch.cuda.synchronize()
+        m.check_device_status()
         return
     dist = None
     if world > 1:
