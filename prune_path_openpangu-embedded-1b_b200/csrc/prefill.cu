@@ -11,8 +11,9 @@
 //   moe_fused_expert_kernel (tl:271-328)    -> gu_gemm_kernel (gathered token rows x the
 //                                             expert's interleaved gate/up rows, SwiGLU and
 //                                             gate weight in the epilogue -> a2 rows) +
-//                                             down_gemm_kernel (a2 x down_t, fp32 reduction
-//                                             into a per-token accumulator) + convert_kernel
+//                                             down_gemm_kernel (a2 x down_t, one fp32 row per
+//                                             pair) + pair_combine_kernel (per token, its rows in
+//                                             expert order)
 // Numerics follow the reference's bf16 rounding points; the per-token combine over experts
 // accumulates in fp32 and rounds once (the reference Triton kernel adds bf16 atomics).
 #include <mutex>
@@ -27,7 +28,7 @@ constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle 
 
 struct PrefillWs {
   size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, pair_token, pair_w,
-      a2, out_acc, status, total;
+      a2, ypart, tok_pairs, tok_k, status, total;
   long long max_pairs, max_tiles;
   int nblocks;
 };
@@ -40,9 +41,6 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   size_t o = 0;
   auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 1024); return r; };
   w.status = take(64);
-  // the fp32 accumulator comes first so its place does not depend on the token count: a
-  // workspace zeroed once and sized for N tokens then serves every call with <= N tokens
-  w.out_acc = take((size_t)N * H * 4);
   w.logits = take((size_t)N * E * 2);
   w.weights = take((size_t)N * E * 2);
   w.blockcnt = take((size_t)w.nblocks * E * 4);
@@ -55,6 +53,9 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   w.pair_token = take((size_t)w.max_pairs * 4);
   w.pair_w = take((size_t)w.max_pairs * 4);
   w.a2 = take((size_t)w.max_pairs * G * 2);
+  w.ypart = take((size_t)w.max_pairs * H * 4);  // fp32 down-projection row of every pair
+  w.tok_pairs = take((size_t)N * E * 4);        // per token: its pairs in expert order
+  w.tok_k = take((size_t)N * 4);
   w.total = o;
   return w;
 }
@@ -224,19 +225,34 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
 // Per token block: (token, expert) pairs in token order within each expert.
 __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, const int* __restrict__ blockoff,
                                const int* __restrict__ exp_off, int* __restrict__ pair_token,
-                               float* __restrict__ pair_w) {
+                               float* __restrict__ pair_w, int* __restrict__ tok_pairs, int* __restrict__ tok_k) {
   // The block's 256 gate-weight rows are consecutive in memory: one coalesced copy into shared
-  // memory (row pitch E + 2 elements against bank conflicts).  Warp w owns experts w, w + 8, ...
-  // and walks the 8 token chunks in order, so each pair's slot is a running ballot prefix.
+  // memory (row pitch E + 2 elements against bank conflicts), plus each token's selection
+  // bitmask.  Warp w owns experts w, w + 8, ... and walks the 8 token chunks in order, so each
+  // pair's slot is a running ballot prefix; the token-side index (its pairs in expert order)
+  // comes from the bitmask.
   extern __shared__ __align__(16) uint8_t sc_smem[];
   const int P = E + 2;
-  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(sc_smem);  // [256][E + 2]
+  __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(sc_smem);          // [256][E + 2]
+  uint32_t* bm = reinterpret_cast<uint32_t*>(sc_smem + (size_t)256 * P * 2);  // [256][8]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
   const uint32_t* src = reinterpret_cast<const uint32_t*>(w + (size_t)t0 * E);
   for (int i = tid; i < nt * E / 2; i += 256) {
     const int r = (2 * i) / E, c = (2 * i) % E;
     *reinterpret_cast<uint32_t*>(ws + r * P + c) = src[i];
+  }
+  __syncthreads();
+  if (tid < nt) {
+    int k = 0;
+    for (int q = 0; q < (E + 31) / 32; ++q) {
+      uint32_t m = 0;
+      for (int b = 0; b < 32 && q * 32 + b < E; ++b)
+        m |= (uint32_t)(__bfloat162float(ws[tid * P + q * 32 + b]) > 0.f) << b;
+      bm[tid * 8 + q] = m;
+      k += __popc(m);
+    }
+    tok_k[t0 + tid] = k;
   }
   __syncthreads();
   for (int e = warp; e < E; e += 8) {
@@ -249,6 +265,9 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int N, int E
         const int pos = run + __popc(b & ((1u << lane) - 1u));
         pair_token[pos] = t0 + r;
         pair_w[pos] = wv;
+        int j = __popc(bm[r * 8 + (e >> 5)] & ((1u << (e & 31)) - 1u));
+        for (int q = 0; q < (e >> 5); ++q) j += __popc(bm[r * 8 + q]);
+        tok_pairs[(size_t)(t0 + r) * E + j] = pos;
       }
       run += __popc(b);
     }
@@ -266,28 +285,29 @@ struct GUArgs {
   const float* pair_w;
   __nv_bfloat16* a2;  // [pairs][G]
   uint32_t* status;
+  int stages;  // pipeline depth (5, or 4 when 2G = 256 rows per B stage)
 };
 
-constexpr int kGUStages = 4;
-constexpr int kGULag = 2;  // cp.async groups kept in flight per producer thread
+constexpr int kGUMaxStages = 5;  // cp.async groups kept in flight per producer thread
 
 __global__ void __launch_bounds__(320, 1)
 gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int S = a.stages, LAG = S - 2;  // cp.async groups kept in flight per producer thread
   const int NB = 2 * a.G;  // interleaved gate/up rows = MMA N
   const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)NB * 128;
   const uint32_t stage_bytes = a_bytes + b_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGUStages * stage_bytes);
-  uint64_t* empty = full + kGUStages;
-  uint64_t* tfull = empty + kGUStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   const int KB = a.H / kBK;
   const int ntiles = *a.ntiles;
   if (tid == 0) {
-    for (int s = 0; s < kGUStages; ++s) { mbar_init(&full[s], 129); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 129); mbar_init(&empty[s], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
     fence_mbar_init();
   }
@@ -308,8 +328,8 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
       const bool real = tok >= 0;
       const __nv_bfloat16* src = a.x + (size_t)(real ? tok : 0) * a.H;
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % kGUStages;
-        mbar_wait(&empty[s], ((it / kGUStages) & 1) ^ 1, a.status);
+        const int s = it % S;
+        mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.status);
         uint8_t* st = smem + s * stage_bytes;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
@@ -319,16 +339,16 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
           mbar_arrive_expect_tx(&full[s], b_bytes);
           tma_load_3d(st + a_bytes, &mapGU, kb * kBK, 0, e * a.G, &full[s]);
         }
-        if (it >= kGULag) {
-          cp_async_wait<kGULag>();
+        if (it >= LAG) {
+          if (LAG == 3) cp_async_wait<3>(); else cp_async_wait<2>();
           fence_proxy_async();
-          mbar_arrive(&full[(it - kGULag) % kGUStages]);
+          mbar_arrive(&full[(it - LAG) % S]);
         }
       }
     }
     cp_async_wait<0>();
     fence_proxy_async();
-    for (int j = max(0, it - kGULag); j < it; ++j) mbar_arrive(&full[j % kGUStages]);
+    for (int j = max(0, it - LAG); j < it; ++j) mbar_arrive(&full[j % S]);
   } else if (warp == 8 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
     int it = 0, tl = 0;
@@ -337,8 +357,8 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
       mbar_wait(&tempty[acc], ((tl >> 1) & 1) ^ 1, a.status);
       tc_fence_after();
       for (int kb = 0; kb < KB; ++kb, ++it) {
-        const int s = it % kGUStages;
-        mbar_wait(&full[s], (it / kGUStages) & 1, a.status);
+        const int s = it % S;
+        mbar_wait(&full[s], (it / S) & 1, a.status);
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + s * stage_bytes);
         const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
@@ -393,20 +413,19 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
 // ======================================================================== down GEMM + combine
 struct DownArgs {
   int H, G, NCW;
+  float* ypart;  // [pairs][H] fp32
   const int* tile_expert;
   const int* tile_row0;
   const int* ntiles;
   const int* pair_token;
-  float* out_acc;  // [N][H] fp32, zero on entry
   uint32_t* status;
 };
 
 constexpr int kDownStages = 2;
-constexpr int kStgPitch = 68;  // floats per staged 64-column row (+16 B against bank conflicts)
 
 __global__ void __launch_bounds__(192, 1)
 down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
-                 const DownArgs a) {
+                 const __grid_constant__ CUtensorMap mapY, const DownArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -423,7 +442,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   uint64_t* tfull = aempty + 1;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 128));
+  uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 1024));
   const int NCH = a.H / a.NCW;
   const int ntiles = *a.ntiles;
   if (tid == 0) {
@@ -476,42 +495,41 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
       }
       umma_commit(aempty);
     }
-  } else if (warp < 4) {  // epilogue: fp32 reduction of each pair row into its token's row
-    // Each thread stages 64 columns of its own row in shared memory and hands them to the TMA
-    // unit as one 256-byte bulk reduce-add into the token's fp32 accumulator row (double
-    // buffered per thread; no cross-thread synchronisation needed).
+  } else if (warp < 4) {  // epilogue: the tile's fp32 rows, stored in pair order
+    // Per 32-column slice: every thread writes its row's 32 values into a 128-byte-swizzled
+    // [128 rows x 32] staging tile (conflict-free), the 4 epilogue warps meet at a named
+    // barrier, and one thread stores the whole 16 KB tile with a single TMA tensor store.
+    // Two staging tiles alternate; a tile is rewritten only after its store has read it.
     const int r = warp * 32 + lane;
-    float* stage = reinterpret_cast<float*>(stg) + (size_t)r * (2 * kStgPitch);
+    uint8_t* stg0 = stg;  // 2 x 16 KB, 1024-byte aligned
     int ch = 0, sub = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int tok = a.pair_token[a.tile_row0[tile] + r];
+      const int row0 = a.tile_row0[tile];
       for (int c = 0; c < NCH; ++c, ++ch) {
         const int acc = ch & 1;
         mbar_wait(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
-        float* dst = a.out_acc + (size_t)(tok < 0 ? 0 : tok) * a.H + c * a.NCW;
-        for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
-          float* buf = stage + (sub & 1) * kStgPitch;
-          bulk_wait_read<1>();  // the reduce that last read this buffer has consumed it
+        for (int c0 = 0; c0 < a.NCW; c0 += 32, ++sub) {
+          uint8_t* buf = stg0 + (sub & 1) * 16384;
+          if (r == 0) bulk_wait_read<1>();
+          named_bar_sync(1, 128);  // the buffer is free
           float v[32];
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32 * h, v);
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(buf + 32 * h + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<float4*>(buf + sw128_offset(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          fence_proxy_async();
+          named_bar_sync(1, 128);  // the tile is complete
+          if (r == 0) {
+            tma_store_2d(&mapY, buf, c * a.NCW + c0, row0);
+            bulk_commit();
           }
-          if (tok >= 0) {
-            fence_proxy_async();
-            bulk_reduce_add_f32(dst + c0, buf, 256);
-          }
-          bulk_commit();
         }
         tc_fence_before();
         mbar_arrive(&tempty[acc]);
       }
     }
-    bulk_wait<0>();
+    if (r == 0) bulk_wait<0>();
   }
   __syncthreads();
   if (warp == 5) {
@@ -520,23 +538,39 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   }
 }
 
-// fp32 accumulator -> bf16 output (one rounding); leaves the accumulator zeroed for the next call
-__global__ void convert_kernel(float4* __restrict__ acc, uint2* __restrict__ out, long long n4) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
-    const float4 v = acc[i];
-    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-    pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    out[i] = pk;
-  }
-}
-
-__global__ void convert_f32_kernel(float4* __restrict__ acc, float4* __restrict__ out, long long n4) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
-    out[i] = acc[i];
-    acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+// Per token: the fp32 rows of its pairs added in expert order (deterministic), rounded once
+// to bf16 (or written as fp32 partial sums for expert-parallel ranks).
+template <bool F32OUT>
+__global__ void pair_combine_kernel(const float4* __restrict__ ypart, const int* __restrict__ tok_pairs,
+                                    const int* __restrict__ tok_k, int E, int H4, void* __restrict__ out) {
+  __shared__ int rows[256];
+  const int t = blockIdx.x;
+  const int k = tok_k[t];
+  for (int j = threadIdx.x; j < k; j += blockDim.x) rows[j] = tok_pairs[(size_t)t * E + j];
+  __syncthreads();
+  for (int c = threadIdx.x; c < H4; c += blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    int j = 0;
+    for (; j + 4 <= k; j += 4) {  // four independent loads in flight, added in order
+      float4 v[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = ypart[(size_t)rows[j + q] * H4 + c];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { s.x += v[q].x; s.y += v[q].y; s.z += v[q].z; s.w += v[q].w; }
+    }
+    for (; j < k; ++j) {
+      const float4 v = ypart[(size_t)rows[j] * H4 + c];
+      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    if (F32OUT) {
+      static_cast<float4*>(out)[(size_t)t * H4 + c] = s;
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      static_cast<uint2*>(out)[(size_t)t * H4 + c] = pk;
+    }
   }
 }
 
@@ -572,6 +606,25 @@ static int make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PPMOE_ERR_CUDA;
+  }
+  return PPMOE_OK;
+}
+
+// fp32 rank-2 map, 128-byte swizzle (32 floats per swizzle row), for tile stores.
+static int make_map_f32(CUtensorMap* m, const void* base, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
+                        const cuuint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return PPMOE_ERR_CUDA;
+  }
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides_bytes, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (fp32) failed (%d)", (int)r);
     return PPMOE_ERR_CUDA;
   }
   return PPMOE_OK;
@@ -657,35 +710,43 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   float* pair_w = reinterpret_cast<float*>(ws + W.pair_w);
   const size_t sc_smem = (size_t)256 * (E + 2) * 2;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
-  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sc_smem + 256 * 8 * 4)));
   count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, N, E, blockcnt);
   scan_kernel<<<1, 256, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
                                  pair_token, pair_w, reinterpret_cast<long long*>(counts));
-  scatter_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w);
+  scatter_kernel<<<W.nblocks, 256, sc_smem + 256 * 8 * 4, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w,
+                                                       reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
   PPMOE_CHECK_CUDA(cudaGetLastError());
 
   // ---- experts
   const int grid = (int)std::min<long long>(nsm, W.max_tiles);
   GUArgs ga{static_cast<const __nv_bfloat16*>(x), H, G, tile_expert, tile_row0, ntiles, pair_token, pair_w,
-            reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status};
-  const size_t g_smem = 1024 + kGUStages * (kTileM * 128 + (size_t)2 * G * 128) + 256;
+            reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status, 2 * G <= 192 ? kGUMaxStages : 4};
+  const size_t g_smem = 1024 + (size_t)ga.stages * (kTileM * 128 + (size_t)2 * G * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g_smem));
   gu_gemm_kernel<<<grid, 320, g_smem, st>>>(mGU, ga);
   PPMOE_CHECK_CUDA(cudaGetLastError());
-  DownArgs da{H, G, NCW, tile_expert, tile_row0, ntiles, pair_token, reinterpret_cast<float*>(ws + W.out_acc), status};
+  CUtensorMap mY;
+  {
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)W.max_pairs}, st2[1] = {(cuuint64_t)H * 4};
+    cuuint32_t b[2] = {32, kTileM};
+    if ((rc = make_map_f32(&mY, ws + W.ypart, d, st2, b))) return rc;
+  }
+  DownArgs da{H, G, NCW, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
   const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
-                        (size_t)kTileM * 2 * kStgPitch * 4 + 128;
+                        2 * 16384 + 1024;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, da);
+  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mY, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());
-  const long long n4 = (long long)N * H / 4;
-  const int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)nsm * 16);
+  int* tok_pairs = reinterpret_cast<int*>(ws + W.tok_pairs);
+  int* tok_k = reinterpret_cast<int*>(ws + W.tok_k);
+  const float4* yp = reinterpret_cast<const float4*>(ws + W.ypart);
   if (mode == kPrefillExperts)
-    convert_f32_kernel<<<cgrid, 256, 0, st>>>(reinterpret_cast<float4*>(ws + W.out_acc), static_cast<float4*>(out), n4);
+    pair_combine_kernel<true><<<N, 128, 0, st>>>(yp, tok_pairs, tok_k, E, H / 4, out);
   else
-    convert_kernel<<<cgrid, 256, 0, st>>>(reinterpret_cast<float4*>(ws + W.out_acc), static_cast<uint2*>(out), n4);
+    pair_combine_kernel<false><<<N, 128, 0, st>>>(yp, tok_pairs, tok_k, E, H / 4, out);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
 }
