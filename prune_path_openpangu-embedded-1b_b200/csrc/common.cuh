@@ -87,6 +87,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking probe of an mbarrier phase (returns at once; try_wait may suspend the thread
+// for a system-defined time window before it re-checks).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  On timeout it records DEVERR_TIMEOUT in *status and
 // returns false; the caller carries on (with garbage data) so that every CTA still reaches
 // every cluster barrier and the launch ends.
@@ -94,8 +105,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   const uint32_t a = smem_u32(bar);
 #pragma unroll 1
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
-    if (i > 4096) __nanosleep(32);
+    if (i < 8192 ? mbar_test_wait(a, parity) : mbar_try_wait(a, parity)) return true;
+    if (i > 16384) __nanosleep(32);
     // once any wait of this launch has given up, stop waiting quickly everywhere else
     if ((i & 1023u) == 1023u && status && *reinterpret_cast<volatile uint32_t*>(status)) return false;
   }

@@ -93,7 +93,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   s.ulist = o;   o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
   s.kbuf = o;    o = (uint32_t)align_up(o + (size_t)kDecWarps * 64 * 4, 128);
-  s.a2 = o;      o = (uint32_t)align_up(o + (size_t)64 * NT * 4, 1024);  // >= max(warps, slots)
+  s.a2 = o;      o = (uint32_t)align_up(o + (size_t)max(64 * NT, kDecWarps * 8 + 32) * 4, 1024);  // >= max(warps, slots); direct-path partials
   s.ring = o;    o += (uint32_t)slots * dec_slot_bytes(H);
   s.total = o;
   return s;
@@ -281,11 +281,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
     if (lane == 0) misc[0] = base;
     __syncwarp();
-    work_range(base);
-    // the router slice / scratch in the ring is dead: every warp passed the barrier above
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    const int win = min(cnt, a.slots);
-    for (int n = lane; n < win; n += 32) issue_neuron(n);
+    PPMOE_TRACE(16);
   }
   // optional side outputs from the first CTA of the grid
   if (blockIdx.x == 0) {
@@ -305,7 +301,29 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   __syncthreads();
-  if (warp != 0) work_range(misc[0]);
+  work_range(misc[0]);
+  // Single-token fast path: the whole CTA range fits the ring (at most 24 neurons).
+  bool fast = false;
+  if constexpr (NT == 1) fast = cnt <= min(a.slots, 24) && (H & 63) == 0;
+  // the router slice / scratch in the ring is dead: every warp passed the barrier above
+  if (fast) {
+    // One bulk copy per neuron into its padded slot (pitch 6H + 32 staggers the banks of
+    // the 8-row fragment loads); tile t (neurons 4t .. 4t+3) completes on bars[t].
+    if (warp == 0 && cnt > 0) {
+      if (lane < (cnt + 3) / 4) mbar_arrive_expect_tx(&bars[lane], (uint32_t)min(4, cnt - 4 * lane) * rec_bytes);
+      __syncwarp();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int n = lane; n < cnt; n += 32) {
+        const int gi = i0 + n, u = gi / G;
+        bulk_g2s(ring + (size_t)n * slotb, a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H,
+                 rec_bytes, &bars[n >> 2], pol);
+      }
+    }
+  } else if (warp == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const int win = min(cnt, a.slots);
+    for (int n = lane; n < win; n += 32) issue_neuron(n);
+  }
   PPMOE_TRACE(6);
 
   float acc[HCH][NT][4];
@@ -316,107 +334,105 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
       for (int q = 0; q < 4; ++q) acc[c][t][q] = 0.f;
 
-  // Wait for the whole first window (the single-token path computes on all of it at once).
-  {
-    const int win = min(cnt, a.slots);
-#pragma unroll 1
-    for (int n = 0; n < win; ++n) mbar_wait(&bars[n], 0u, a.status);
-  }
-  PPMOE_TRACE(7);
-
-  // Single-token fast path, whole window resident: every warp takes neurons w, w+12, ...
-  // two at a time with the token's activations held in registers, one barrier, then every
-  // thread applies all down rows to its output columns.
-  bool fast = false;
-  if constexpr (NT == 1) fast = cnt <= a.slots && H <= 2048;
   if (fast) {
-    // gate/up GEMV on the tensor cores: rows (neuron n gate, neuron n up) of 8 neurons form a
-    // 16-row A tile (ldmatrix from the padded ring), the token is column 0 of an 8-column B
-    // tile; warps split the tiles and the K range, partial sums meet in shared memory.
-    const int T = (cnt + 7) >> 3;
-    const int KS = kDecWarps / T;
-    const int ksteps = H / 16;
-    float* pgu = reinterpret_cast<float*>(smem + L.kbuf);  // [KS][T*16] (reuses the selection buffer)
-    if (warp < T * KS) {
-      const int tile = warp % T, ks = warp / T;
-      const int k0 = (ksteps * ks) / KS, k1 = (ksteps * (ks + 1)) / KS;
-      const int r = lane & 15;
-      int nr = tile * 8 + (r >> 1);
-      if (nr >= cnt) nr = 0;  // padding rows read a valid row; results are ignored
-      const uint32_t arow = smem_u32(ring + (size_t)nr * slotb + (r & 1) * rowp) + (lane >> 4) * 16;
-      const uint32_t* x32 = reinterpret_cast<const uint32_t*>(xs);
-      // Four k-steps per round: all fragment loads of the round are issued before its MMAs
-      // (the loads are not volatile, so they can be scheduled ahead), two accumulator chains.
-      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      auto mma = [&](float (&dc)[4], const uint32_t (&af)[4], uint32_t b0, uint32_t b1) {
-        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-                     "{%0,%1,%2,%3};"
-                     : "+f"(dc[0]), "+f"(dc[1]), "+f"(dc[2]), "+f"(dc[3])
-                     : "r"(af[0]), "r"(af[1]), "r"(af[2]), "r"(af[3]), "r"(b0), "r"(b1));
-      };
-      for (int kk = k0; kk < k1; kk += 4) {
-        uint32_t af[4][4], bf[4][2];
+    // Single-token tensor-core path.  Gate/up: D[16 x 8] = A[16 x 16] * B[16 x 8] per k-step
+    // with mma.sync m16n8k16: A row 0 is the token (other rows zero); B's 8 columns are the
+    // gate/up rows of one tile of 4 neurons (column 2i: gate of neuron 4 t + i, 2i+1: its up
+    // row).  Inside each 16-wide k-step the k order is permuted identically for A and B
+    // (fragment positions 2q, 2q+1, 2q+8, 2q+9 <- elements 4q .. 4q+3), so each lane's B
+    // fragment is one 8-byte shared load; the dot product is unchanged.  Warp w takes tile
+    // w % T and k-part w / T of KS = 12 / T parts and waits only for its tile's copies; the
+    // KS part sums meet in shared memory in part order.  Down: thread tid applies every
+    // neuron's down row to hidden columns 4 tid .. 4 tid + 3 (fp32 FMA, loads ahead of FMAs).
+    const int T = (cnt + 3) >> 2;  // row tiles, <= 6
+    const int KS = kDecWarps / T;  // k-parts per tile
+    const int ksteps = H >> 4;
+    const int tile = warp % T, part = warp / T;
+    const int g8 = lane >> 2, q = lane & 3;
+    float* kpart = reinterpret_cast<float*>(smem + L.a2);  // [KS][T][8]
+    if (part < KS) {
+      const int k0 = (ksteps * part) / KS, k1 = (ksteps * (part + 1)) / KS;
+      const int nr = min(4 * tile + (g8 >> 1), cnt - 1);  // padding columns read a valid row
+      const uint32_t brow = smem_u32(ring + (size_t)nr * slotb + (g8 & 1) * rowp) + 8 * q;
+      const uint32_t xrow = smem_u32(xs) + 8 * q;
+      float d[4][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int k = min(kk + q, k1 - 1);
-          asm("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-              : "=r"(af[q][0]), "=r"(af[q][1]), "=r"(af[q][2]), "=r"(af[q][3]) : "r"(arow + k * 32));
-          bf[q][0] = lane < 4 ? x32[k * 8 + lane] : 0u;
-          bf[q][1] = lane < 4 ? x32[k * 8 + 4 + lane] : 0u;
+      for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
+      mbar_wait(&bars[tile], 0u, a.status);
+      #pragma unroll 1
+      for (int kk = k0; kk < k1; kk += 4) {
+        uint2 xa[4], bv[4];
+#pragma unroll
+        for (int s2 = 0; s2 < 4; ++s2) {
+          const int k = min(kk + s2, k1 - 1);
+          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv[s2].x), "=r"(bv[s2].y) : "r"(brow + 32 * k));
+          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(xa[s2].x), "=r"(xa[s2].y) : "r"(xrow + 32 * k));
+          // only A row 0 (lanes 0-3) carries the token; steps past k1 contribute nothing
+          if (lane >= 4 || kk + s2 >= k1) xa[s2] = make_uint2(0u, 0u);
         }
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (kk + q < k1) mma(d[q & 1], af[q], bf[q][0], bf[q][1]);
+        for (int s2 = 0; s2 < 4; ++s2)
+          asm volatile(
+              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(d[s2][0]), "+f"(d[s2][1]), "+f"(d[s2][2]), "+f"(d[s2][3])
+              : "r"(xa[s2].x), "r"(0u), "r"(xa[s2].y), "r"(0u), "r"(bv[s2].x), "r"(bv[s2].y));
       }
-      const float d0 = d[0][0] + d[1][0], d2 = d[0][2] + d[1][2];
-      if ((lane & 3) == 0) {  // column 0: rows lane/4 and lane/4 + 8
-        pgu[ks * T * 16 + tile * 16 + (lane >> 2)] = d0;
-        pgu[ks * T * 16 + tile * 16 + (lane >> 2) + 8] = d2;
+      if (lane < 4) {
+        kpart[(part * T + tile) * 8 + 2 * q] = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);      // gate
+        kpart[(part * T + tile) * 8 + 2 * q + 1] = (d[0][1] + d[1][1]) + (d[2][1] + d[3][1]);  // up
       }
     }
+    PPMOE_TRACE(19);
     __syncthreads();
+    float* a2k = kpart + kDecWarps * 8;
+    PPMOE_TRACE(20);
     if (tid < cnt) {
-      const int n = tid, tile = n >> 3, rg = 2 * (n & 7);
-      float g = 0.f, u = 0.f;
-      for (int ks = 0; ks < KS; ++ks) {  // fixed order
-        g += pgu[ks * T * 16 + tile * 16 + rg];
-        u += pgu[ks * T * 16 + tile * 16 + rg + 1];
+      float g = 0.f, uu = 0.f;
+      #pragma unroll 1
+      for (int p = 0; p < KS; ++p) {  // part order
+        g += kpart[(p * T + (tid >> 2)) * 8 + 2 * (tid & 3)];
+        uu += kpart[(p * T + (tid >> 2)) * 8 + 2 * (tid & 3) + 1];
       }
-      const float gb = bf16r(g), ub = bf16r(u);
+      const float gb = bf16r(g), ub = bf16r(uu);
       const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
-      a2s[n] = bf16r(bf16r(sb * ub) * ws[ulist[(i0 + n) / G]]);
+      a2k[tid] = bf16r(bf16r(sb * ub) * ws[ulist[(i0 + tid) / G]]);
     }
     __syncthreads();
 #pragma unroll
     for (int c = 0; c < HCH; ++c) {
       const int h4 = tid + c * kDecThreads;
       if (h4 < H / 4) {
-#pragma unroll 1
-        for (int m0 = 0; m0 < cnt; m0 += 4) {
-          uint2 dv[4];
+        #pragma unroll 1
+        for (int m0 = 0; m0 < cnt; m0 += 8) {
+          uint2 dv[8];
+          float av[8];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int m = min(m0 + q, cnt - 1);
-            dv[q] = *reinterpret_cast<const uint2*>(
-                reinterpret_cast<const __nv_bfloat16*>(ring + (size_t)m * slotb + 2 * rowp) + h4 * 4);
+          for (int i = 0; i < 8; ++i) {
+            const int m = min(m0 + i, cnt - 1);
+            dv[i] = *reinterpret_cast<const uint2*>(ring + (size_t)m * slotb + 2 * rowp + 8 * h4);
+            av[i] = m0 + i < cnt ? a2k[m0 + i] : 0.f;  // 0 * finite weight adds exactly nothing
           }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            if (m0 + q < cnt) {
-              const float av = a2s[m0 + q];
-              const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].x));
-              const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[q].y));
-              acc[c][0][0] = fmaf(av, d01.x, acc[c][0][0]);
-              acc[c][0][1] = fmaf(av, d01.y, acc[c][0][1]);
-              acc[c][0][2] = fmaf(av, d23.x, acc[c][0][2]);
-              acc[c][0][3] = fmaf(av, d23.y, acc[c][0][3]);
-            }
+          for (int i = 0; i < 8; ++i) {
+            const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[i].x));
+            const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[i].y));
+            acc[c][0][0] = fmaf(av[i], d01.x, acc[c][0][0]);
+            acc[c][0][1] = fmaf(av[i], d01.y, acc[c][0][1]);
+            acc[c][0][2] = fmaf(av[i], d23.x, acc[c][0][2]);
+            acc[c][0][3] = fmaf(av[i], d23.y, acc[c][0][3]);
           }
         }
       }
     }
-    __syncthreads();
+  } else {
+    // Wait for the whole first window before the batched loop reuses slots.
+    const int win = min(cnt, a.slots);
+#pragma unroll 1
+    for (int n = 0; n < win; ++n) mbar_wait(&bars[n], 0u, a.status);
   }
+  PPMOE_TRACE(7);
+
   for (int b0 = 0; b0 < (fast ? 0 : cnt); b0 += kDecWarps) {
     const int n = b0 + warp;
 #pragma unroll
@@ -544,16 +560,46 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   // peers may still read this CTA's shared memory: arrive now, wait before exiting
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // ---- 4c. the last cluster to finish this column slice sums all cluster partials
+  // The barrier orders every thread's partial store before thread 0's release; the
+  // acquire side of the same atomic orders the last cluster's reads after all of them.
   __syncthreads();
   if (tid == 0) {
-    __threadfence();
-    const uint32_t old = atomicAdd(&a.counters[rank], 1u);
+    uint32_t old;
+    asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + rank) : "memory");
     misc[1] = (old == (uint32_t)nclusters - 1u);
   }
   __syncthreads();
   PPMOE_TRACE(10);
-  if (misc[1]) {
-    __threadfence();
+  const int nel = N * (HS / 4);  // float4 elements of this rank's column slice
+  if (misc[1] && nel * nclusters <= 2 * kDecThreads) {
+    // every cluster partial of the slice in one round of loads, then sums in cluster order
+    float4* gat = reinterpret_cast<float4*>(ring + align_up((size_t)N * H * 4, 128));
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int j = tid + r * kDecThreads;
+      if (j < nel * nclusters) {
+        const int c = j / nel, i = j - c * nel;
+        const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
+        gat[j] = __ldcg(reinterpret_cast<const float4*>(a.cpart + ((size_t)c * N + t) * H + h));
+      }
+    }
+    __syncthreads();
+    if (tid < nel) {
+      const int t = tid / (HS / 4), h = rank * HS + (tid % (HS / 4)) * 4;
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      #pragma unroll 1
+      for (int c = 0; c < nclusters; ++c) {
+        const float4 v = gat[c * nel + tid];
+        s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+      }
+      __nv_bfloat162 lo = __floats2bfloat162_rn(s4.x, s4.y), hi = __floats2bfloat162_rn(s4.z, s4.w);
+      uint2 pk;
+      pk.x = *reinterpret_cast<uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(a.out + (size_t)t * H + h) = pk;
+    }
+    if (tid == 0) a.counters[rank] = 0u;  // re-arm for the next launch
+  } else if (misc[1]) {
     #pragma unroll 1
     for (int i = tid; i < N * (HS / 4); i += kDecThreads) {
       const int t = i / (HS / 4), h = rank * HS + (i % (HS / 4)) * 4;
