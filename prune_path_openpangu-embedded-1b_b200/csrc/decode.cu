@@ -301,10 +301,24 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   __syncthreads();
+  PPMOE_TRACE(17);
   work_range(misc[0]);
   // Single-token fast path: the whole CTA range fits the ring (at most 24 neurons).
-  bool fast = false;
+  bool fast = false, tcb = false;
   if constexpr (NT == 1) fast = cnt <= min(a.slots, 24) && (H & 63) == 0;
+  if constexpr (NT >= 2 && HCH == 1) tcb = (H % 384) == 0 && a.slots >= 16;
+  // batched path: round r = neurons [8r, 8r + 8) into slots 8 (r & 1) .. +8, on bars[r & 1]
+  auto issue_round = [&](int r) {
+    const int nr = min(8, cnt - 8 * r);
+    if (lane == 0) mbar_arrive_expect_tx(&bars[r & 1], (uint32_t)nr * rec_bytes);
+    __syncwarp();
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (lane < nr) {
+      const int gi = i0 + 8 * r + lane, u = gi / G;
+      bulk_g2s(ring + (size_t)(8 * (r & 1) + lane) * slotb,
+               a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H, rec_bytes, &bars[r & 1], pol);
+    }
+  };
   // the router slice / scratch in the ring is dead: every warp passed the barrier above
   if (fast) {
     // One bulk copy per neuron into its padded slot (pitch 6H + 32 staggers the banks of
@@ -318,6 +332,11 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         bulk_g2s(ring + (size_t)n * slotb, a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H,
                  rec_bytes, &bars[n >> 2], pol);
       }
+    }
+  } else if (tcb) {
+    if (warp == 0) {
+      if (cnt > 0) issue_round(0);
+      if (cnt > 8) issue_round(1);
     }
   } else if (warp == 0) {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -359,6 +378,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
       for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
       mbar_wait(&bars[tile], 0u, a.status);
+      PPMOE_TRACE(18);
       #pragma unroll 1
       for (int kk = k0; kk < k1; kk += 4) {
         uint2 xa[4], bv[4];
@@ -388,17 +408,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     float* a2k = kpart + kDecWarps * 8;
     PPMOE_TRACE(20);
     if (tid < cnt) {
-      float g = 0.f, uu = 0.f;
-      #pragma unroll 1
-      for (int p = 0; p < KS; ++p) {  // part order
-        g += kpart[(p * T + (tid >> 2)) * 8 + 2 * (tid & 3)];
-        uu += kpart[(p * T + (tid >> 2)) * 8 + 2 * (tid & 3) + 1];
+      float gp[kDecWarps], up[kDecWarps];
+#pragma unroll
+      for (int p = 0; p < kDecWarps; ++p) {
+        const int o = (min(p, KS - 1) * T + (tid >> 2)) * 8 + 2 * (tid & 3);
+        gp[p] = kpart[o];
+        up[p] = kpart[o + 1];
       }
+      float g = 0.f, uu = 0.f;
+#pragma unroll
+      for (int p = 0; p < kDecWarps; ++p)  // part order
+        if (p < KS) { g += gp[p]; uu += up[p]; }
       const float gb = bf16r(g), ub = bf16r(uu);
       const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
       a2k[tid] = bf16r(bf16r(sb * ub) * ws[ulist[(i0 + tid) / G]]);
     }
     __syncthreads();
+    PPMOE_TRACE(21);
 #pragma unroll
     for (int c = 0; c < HCH; ++c) {
       const int h4 = tid + c * kDecThreads;
@@ -425,6 +451,131 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         }
       }
     }
+  } else if (tcb) {
+    // Batched tensor-core path (2..16 tokens).  Rounds of 8 neurons (two tiles of 4),
+    // double-buffered over ring slots 0-15; round r's copies complete on bars[r & 1].
+    // Gate/up: mma.sync m16n8k16 with the tokens as A rows and, per tile, the gate/up rows
+    // of 4 neurons as B columns (same permuted-k 8-byte fragments as the single-token path);
+    // warp w owns k-steps [w KW, (w+1) KW) of every tile and keeps its x fragments in
+    // registers for the whole launch, so the x region is reused for the per-warp partials
+    // [12][2][NT][8] (summed in warp order).  Down: mma.sync m16n8k8, A = a2 [16 tokens x 8
+    // neurons] (bf16, zero for tokens that did not select the neuron's expert), B = the
+    // round's down rows read transposed by ldmatrix; warp w owns hidden columns
+    // [H/12 w, H/12 (w + 1)) and accumulates them over all rounds in registers.
+    constexpr int kMaxKW = 8;  // k-steps per warp (H <= 1536)
+    const int KW = (H >> 4) / kDecWarps;
+    const int g8 = lane >> 2, q = lane & 3;
+    uint2 xa[kMaxKW][2];  // A fragments: token rows g8 and g8 + 8
+#pragma unroll
+    for (int s2 = 0; s2 < kMaxKW; ++s2) {
+      const int k = warp * KW + min(s2, KW - 1);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = g8 + 8 * hh;
+        xa[s2][hh] = (t < NT && s2 < KW) ? *reinterpret_cast<const uint2*>(xs + (size_t)t * H + 16 * k + 4 * q)
+                                          : make_uint2(0u, 0u);
+      }
+    }
+    __nv_bfloat16* a2t = reinterpret_cast<__nv_bfloat16*>(smem + L.a2);  // [16 tokens][8 neurons]
+    if (tid < 64) reinterpret_cast<uint32_t*>(a2t)[tid] = 0u;
+    __syncthreads();  // every warp holds its x fragments: the x region becomes the partials
+    float* kp = reinterpret_cast<float*>(xs);
+    float dacc[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) dacc[j][0] = dacc[j][1] = dacc[j][2] = dacc[j][3] = 0.f;
+    const int colw = H / kDecWarps;  // hidden columns per warp (multiple of 32)
+    const int rounds = (cnt + 7) >> 3;
+    #pragma unroll 1
+    for (int r = 0; r < rounds; ++r) {
+      const int nr = min(8, cnt - 8 * r);
+      const uint8_t* sb = ring + (size_t)(8 * (r & 1)) * slotb;
+      mbar_wait(&bars[r & 1], (uint32_t)((r >> 1) & 1), a.status);
+      // ---- gate/up
+      float d[2][4];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0.f;
+      uint32_t brow[2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+        brow[t] = smem_u32(sb + (size_t)min(4 * t + (g8 >> 1), nr - 1) * slotb + (g8 & 1) * rowp) + 8 * q +
+                  32 * warp * KW;
+#pragma unroll
+      for (int s2 = 0; s2 < kMaxKW; ++s2) {
+        if (s2 < KW) {
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            uint2 bv;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv.x), "=r"(bv.y) : "r"(brow[t] + 32 * s2));
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+f"(d[t][0]), "+f"(d[t][1]), "+f"(d[t][2]), "+f"(d[t][3])
+                : "r"(xa[s2][0].x), "r"(xa[s2][1].x), "r"(xa[s2][0].y), "r"(xa[s2][1].y), "r"(bv.x), "r"(bv.y));
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (g8 < NT)
+          *reinterpret_cast<float2*>(kp + ((warp * 2 + t) * NT + g8) * 8 + 2 * q) = make_float2(d[t][0], d[t][1]);
+        if (g8 + 8 < NT)
+          *reinterpret_cast<float2*>(kp + ((warp * 2 + t) * NT + g8 + 8) * 8 + 2 * q) = make_float2(d[t][2], d[t][3]);
+      }
+      __syncthreads();
+      // ---- SwiGLU + gate weight per (token, neuron); warp order over the k partials
+      if (tid < NT * 8) {
+        const int t = tid >> 3, n = tid & 7, tl = n >> 2, i = n & 3;
+        float g = 0.f, uu = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w) {
+          const float2 v = *reinterpret_cast<const float2*>(kp + ((w * 2 + tl) * NT + t) * 8 + 2 * i);
+          g += v.x;
+          uu += v.y;
+        }
+        float av = 0.f;
+        if (t < N && n < nr) {
+          const float gb = bf16r(g), ub = bf16r(uu);
+          const float sbv = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+          av = bf16r(sbv * ub) * ws[t * E + ulist[(i0 + 8 * r + n) / G]];     // 0 if not selected
+        }
+        a2t[t * 8 + n] = __float2bfloat16_rn(av);
+      }
+      __syncthreads();
+      // ---- down: out[16 x 128 w..] += a2[16 x 8] * Wd[8 x ...]
+      uint32_t af0, af1;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                   : "=r"(af0), "=r"(af1) : "r"(smem_u32(a2t) + (lane & 15) * 16));
+      const uint32_t drow = smem_u32(sb + (size_t)min(lane & 7, nr - 1) * slotb + 2 * rowp) +
+                            (uint32_t)(colw * warp + 8 * (lane >> 3)) * 2;
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4) {
+        if (32 * j4 >= colw) break;
+        uint32_t b0, b1, b2, b3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(drow + j4 * 64));
+        const uint32_t bb[4] = {b0, b1, b2, b3};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+          asm volatile(
+              "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+              : "+f"(dacc[4 * j4 + jj][0]), "+f"(dacc[4 * j4 + jj][1]), "+f"(dacc[4 * j4 + jj][2]),
+                "+f"(dacc[4 * j4 + jj][3])
+              : "r"(af0), "r"(af1), "r"(bb[jj]));
+      }
+      __syncthreads();  // the round's slots and a2 are consumed
+      if (warp == 0 && r + 2 < rounds) issue_round(r + 2);
+    }
+    // CTA partial straight from the fragments: column tile j of warp w covers hidden
+    // columns H/12 w + 8 j + 2q, +1 for tokens g8 (c0, c1) and g8 + 8 (c2, c3)
+    float* redt = reinterpret_cast<float*>(ring);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (8 * j >= colw) break;
+      const int h = colw * warp + 8 * j + 2 * q;
+      if (g8 < N) *reinterpret_cast<float2*>(redt + (size_t)g8 * H + h) = make_float2(dacc[j][0], dacc[j][1]);
+      if (g8 + 8 < N)
+        *reinterpret_cast<float2*>(redt + (size_t)(g8 + 8) * H + h) = make_float2(dacc[j][2], dacc[j][3]);
+    }
   } else {
     // Wait for the whole first window before the batched loop reuses slots.
     const int win = min(cnt, a.slots);
@@ -433,7 +584,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   }
   PPMOE_TRACE(7);
 
-  for (int b0 = 0; b0 < (fast ? 0 : cnt); b0 += kDecWarps) {
+  for (int b0 = 0; b0 < ((fast || tcb) ? 0 : cnt); b0 += kDecWarps) {
     const int n = b0 + warp;
 #pragma unroll
     for (int t = 0; t < NT; ++t)
@@ -534,7 +685,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
   for (int c = 0; c < HCH; ++c) {
     const int h4 = tid + c * kDecThreads;
-    if (h4 < H / 4) {
+    if (!tcb && h4 < H / 4) {  // the batched tensor-core path wrote its partial already
 #pragma unroll
       for (int t = 0; t < NT; ++t)
         if (t < N)
