@@ -7,19 +7,20 @@
 // Grid: C clusters x 8 CTAs (C = the number of 8-CTA clusters the GPU co-schedules), 384
 // threads per CTA, one CTA per SM.
 //
-//  1. Router.  Rank r of every cluster loads rows [r*H/8, (r+1)*H/8) of router_he
-//     ([H][E], contiguous) with one bulk copy, computes partial logits for all tokens in a
-//     fixed order, and the 8 partials are combined over distributed shared memory in rank
-//     order.  Every cluster computes the same logits with the same operation order, so every
-//     CTA holds bit-identical selections without any grid-wide barrier.
+//  1. Router.  Rank r of every cluster computes the logits of experts [r*E/8, (r+1)*E/8)
+//     for all tokens on the tensor cores (their router_eh rows arrive by bulk copy); the
+//     ranks' logits are exchanged over distributed shared memory.  Every cluster computes the
+//     same logits with the same operation order, so every CTA holds bit-identical
+//     selections without any grid-wide barrier.
 //  2. Selection (select.cuh), redundantly in every CTA: gate weights, union of selected
 //     experts, per-expert token bitmask.
 //  3. Experts.  The union's neurons (|U| * G) are split evenly over all CTAs of the grid.
 //     Each neuron is one contiguous 3*H*2-byte record (gate row | up row | down row) that
-//     a bulk copy streams into a ring of shared-memory slots; 12 warps each compute one
-//     neuron's gate/up dot products for the tokens that selected its expert
-//     (g,u -> bf16; s=bf16(silu(g)); a=bf16(s*u); a2=bf16(a*w)), then all threads apply the
-//     12 down rows to their fp32 output accumulators (4 hidden columns x tokens each).
+//     a bulk copy streams into a ring of shared-memory slots.  One token: gate/up GEMV on the
+//     tensor cores per 4-neuron tile, SwiGLU, fp32 down rows by hidden column.  2..16 tokens
+//     (H % 384 == 0): rounds of 8 neurons, gate/up and down both on the tensor cores.
+//     Otherwise a CUDA-core path (one neuron per warp, tokens that selected its expert).
+//     Rounding points everywhere: g,u -> bf16; s=bf16(silu(g)); a=bf16(s*u); a2=bf16(a*w).
 //  4. Reduction.  The 8 CTA partials of a cluster are summed over distributed shared
 //     memory (rank order) into one partial per cluster in global scratch; per 1/8-slice of
 //     the hidden dimension an arrival counter elects the last cluster, whose CTA sums the
@@ -44,7 +45,7 @@ constexpr int kMaxClusters = 32;  // workspace sizing (148 SMs -> at most 18 clu
 struct DecodeArgs {
   const __nv_bfloat16* x;
   int N;
-  const __nv_bfloat16* router_he;  // [H][E]
+  const __nv_bfloat16* router_eh;  // [E][H]
   const __nv_bfloat16* experts;    // [E][G][3][H]
   int H, E, G;
   float tau_b;
@@ -85,7 +86,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   DecSmem s;
   uint32_t o = 0;
   s.bars = o;    o += 8 * 64;                                   // <= 63 slot barriers + 1
-  s.x = o;       o = (uint32_t)align_up(o + (size_t)NT * H * 2, 128);
+  s.x = o;       o = (uint32_t)align_up(o + (size_t)NT * (H + 8) * 2, 128);
   s.part = o;    o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
   s.lg = o;      o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
   s.w = o;       o = (uint32_t)align_up(o + (size_t)NT * E * 4, 128);
@@ -108,7 +109,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   const int cid = blockIdx.x / kCluster;
   const int nclusters = gridDim.x / kCluster;
   const int H = a.H, E = a.E, G = a.G, N = a.N;
-  const int HS = H / kCluster;  // router rows / output columns owned by this rank
+  const int HS = H / kCluster;  // output columns owned by this rank in the reduction
+  const int XP = H + 8;          // token row pitch in shared memory (elements)
   const DecSmem L = dec_smem(NT, H, E, a.slots);
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
@@ -132,77 +134,129 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     fence_mbar_init();
   }
   __syncthreads();
-  const uint32_t rs_bytes = (uint32_t)HS * (uint32_t)E * 2u;
-  const uint32_t x_bytes = (uint32_t)N * (uint32_t)H * 2u;
-  __nv_bfloat16* rs = reinterpret_cast<__nv_bfloat16*>(ring);  // router slice aliases the ring
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_in, rs_bytes + x_bytes);
-    bulk_g2s(rs, a.router_he + (size_t)rank * HS * E, rs_bytes, bar_in, policy_evict_last());
+  // Router operands.  Rank r owns experts [r EPR, (r+1) EPR) (EPR = E / 8): their router_eh
+  // rows (H contiguous bf16 each) land in padded ring slots (pitch 2H + 16 bytes) and the
+  // token rows in xs at pitch XP = H + 8, so every 8-row fragment load below is
+  // bank-conflict free.  Router rows are weights (legal before the PDL wait); x is not.
+  const int EPR = E / kCluster;
+  const uint32_t rrow = 2u * (uint32_t)H + 16u;
+  const uint32_t h_bytes = 2u * (uint32_t)H;
+  uint8_t* rsl = ring;  // router slots alias the ring
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(bar_in, (uint32_t)(EPR + N) * h_bytes);
+    __syncwarp();
+    for (int e = lane; e < EPR; e += 32)
+      bulk_g2s(rsl + (size_t)e * rrow, a.router_eh + (size_t)(rank * EPR + e) * H, h_bytes, bar_in,
+               policy_evict_last());
   }
   if (a.pdl) pdl_wait();
-  if (tid == 0) bulk_g2s(xs, a.x, x_bytes, bar_in, policy_evict_first());
-  // zero-fill padded token rows so the router partials stay finite
+  if (warp == 0)
+    for (int t = lane; t < N; t += 32)
+      bulk_g2s(xs + (size_t)t * XP, a.x + (size_t)t * H, h_bytes, bar_in, policy_evict_first());
+  // zero-fill padded token rows so that their (ignored) logits stay finite
   #pragma unroll 1
-  for (int i = N * H + tid; i < NT * H; i += kDecThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = tid; i < (NT - N) * XP; i += kDecThreads) xs[(size_t)N * XP + i] = __float2bfloat16_rn(0.f);
   #pragma unroll 1
   for (int i = tid; i < E; i += kDecThreads) tokmask[i] = 0u;
   mbar_wait(bar_in, 0, a.status);
   PPMOE_TRACE(1);
 
-  // ---- 1. router partial over this rank's K-slice.  The E/2 expert pairs are split into
-  // PB blocks of 32 (lane = pair within block); warp w takes pair block w % PB and rows
-  // k = g, g + KG, ... with g = w / PB.  The KG row-group partials are then summed in group
-  // order, so the operation order is fixed.
-  {
-    const int E2 = E >> 1;
-    const int PB = (E2 + 31) >> 5;
-    const int KG = max(1, kDecWarps / PB);
-    float* scratch = reinterpret_cast<float*>(ring + align_up(rs_bytes, 128));  // [KG][NT][E]
-    const __nv_bfloat162* rs2 = reinterpret_cast<const __nv_bfloat162*>(rs);
-    const int pb = warp % PB, g = warp / PB;
-    const int ep = pb * 32 + lane;
-    if (g < KG && ep < E2) {
-      float2 acc[NT];
+  // ---- 1. this rank's experts' logits on the tensor cores: D[16 tokens x 8 experts] per
+  // expert tile, mma.sync m16n8k16 with the same permuted-k 8-byte fragments as the expert
+  // GEMVs (A = token rows, B = router rows).  Warp w takes k-steps [w ks / 12, (w+1) ks / 12)
+  // of every tile; the per-warp partials are summed in warp order, so every cluster computes
+  // bit-identical logits for the rank's experts.
+  if (NT == 1) {
+    // One token: CUDA-core dot products.  Lane (e8 = lane % 8, k-quarter = lane / 8) of
+    // warp w covers 8 elements of every 32-element chunk of warp w's k-range for expert
+    // 8 j + e8; quarters meet by shuffle (fixed order), warps in warp order.
+    const int e8 = lane & 7, kq = lane >> 3;
+    const int nch = H >> 5;  // 32-element chunks; warp w takes [w nch / 12, (w+1) nch / 12)
+    const int kb = 32 * ((nch * warp) / kDecWarps), ke = 32 * ((nch * (warp + 1)) / kDecWarps);
+    float* rpart = reinterpret_cast<float*>(ring + align_up((size_t)EPR * rrow, 128));  // [12][EPR]
+    #pragma unroll 1
+    for (int j = 0; j < EPR; j += 8) {
+      const int e = min(j + e8, EPR - 1);
+      const __nv_bfloat16* rr = reinterpret_cast<const __nv_bfloat16*>(rsl + (size_t)e * rrow);
+      float s0 = 0.f, s1 = 0.f;
+      #pragma unroll 1
+      for (int k = kb + kq * 8; k < ke; k += 32) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(rr + k);
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
+        const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+        const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] = make_float2(0.f, 0.f);
-#pragma unroll 4
-      for (int k = g; k < HS; k += KG) {
-        const float2 r = __bfloat1622float2(rs2[(size_t)k * E2 + ep]);
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const float xv = __bfloat162float(xs[t * H + rank * HS + k]);
-          acc[t].x = fmaf(xv, r.x, acc[t].x);
-          acc[t].y = fmaf(xv, r.y, acc[t].y);
+        for (int i = 0; i < 4; ++i) {
+          const float2 rf = __bfloat1622float2(rp[i]), xf = __bfloat1622float2(xp[i]);
+          if (i & 1) s1 = fmaf(xf.y, rf.y, fmaf(xf.x, rf.x, s1));
+          else s0 = fmaf(xf.y, rf.y, fmaf(xf.x, rf.x, s0));
         }
       }
+      float v = s0 + s1;
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (kq == 0 && j + e8 < EPR) rpart[warp * EPR + j + e8] = v;
+    }
+    __syncthreads();
+    for (int e = tid; e < EPR; e += kDecThreads) {
+      float s = 0.f;
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
-        *reinterpret_cast<float2*>(scratch + (g * NT + t) * E + 2 * ep) = acc[t];
+      for (int w = 0; w < kDecWarps; ++w) s += rpart[w * EPR + e];  // warp order
+      part[e] = s;
+    }
+  } else {
+    const int NTL = (EPR + 7) >> 3;  // expert tiles
+    const int ks = H >> 4;
+    const int k0 = (ks * warp) / kDecWarps, k1 = (ks * (warp + 1)) / kDecWarps;
+    const int g8 = lane >> 2, q = lane & 3;
+    float* rpart = reinterpret_cast<float*>(ring + align_up((size_t)EPR * rrow, 128));  // [12][NT][8 NTL]
+    #pragma unroll 1
+    for (int tl = 0; tl < NTL; ++tl) {
+      const uint32_t brow = smem_u32(rsl + (size_t)min(8 * tl + g8, EPR - 1) * rrow) + 8 * q;
+      const uint32_t xr0 = smem_u32(xs + (size_t)min(g8, NT - 1) * XP) + 8 * q;
+      const uint32_t xr1 = smem_u32(xs + (size_t)min(g8 + 8, NT - 1) * XP) + 8 * q;
+      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      #pragma unroll 2
+      for (int k = k0; k < k1; ++k) {
+        uint2 bv, a0 = make_uint2(0u, 0u), a1 = make_uint2(0u, 0u);
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv.x), "=r"(bv.y) : "r"(brow + 32 * k));
+        if (g8 < NT) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a0.x), "=r"(a0.y) : "r"(xr0 + 32 * k));
+        if (g8 + 8 < NT) asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a1.x), "=r"(a1.y) : "r"(xr1 + 32 * k));
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[k & 1][0]), "+f"(d[k & 1][1]), "+f"(d[k & 1][2]), "+f"(d[k & 1][3])
+            : "r"(a0.x), "r"(a1.x), "r"(a0.y), "r"(a1.y), "r"(bv.x), "r"(bv.y));
+      }
+      const int e0 = 8 * tl + 2 * q;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int t = g8 + 8 * hh;
+        if (t < NT)
+          *reinterpret_cast<float2*>(rpart + ((size_t)warp * NT + t) * (8 * NTL) + e0) =
+              make_float2(d[0][2 * hh] + d[1][2 * hh], d[0][2 * hh + 1] + d[1][2 * hh + 1]);
+      }
     }
     __syncthreads();
     #pragma unroll 1
-    for (int i = tid; i < NT * E; i += kDecThreads) {
-      float v[kDecWarps];
-#pragma unroll
-      for (int q = 0; q < kDecWarps; ++q) v[q] = q < KG ? scratch[q * NT * E + i] : 0.f;
+    for (int i = tid; i < NT * EPR; i += kDecThreads) {
+      const int t = i / EPR, e = i - t * EPR;
       float s = 0.f;
 #pragma unroll
-      for (int q = 0; q < kDecWarps; ++q) s += v[q];  // group order; trailing zeros are exact
-      part[i] = s;
+      for (int w = 0; w < kDecWarps; ++w) s += rpart[((size_t)w * NT + t) * (8 * NTL) + e];  // warp order
+      part[i] = s;  // [NT][EPR]
     }
   }
   PPMOE_TRACE(2);
-  cluster.sync();  // partials visible cluster-wide
+  cluster.sync();  // every rank's expert logits visible cluster-wide
   PPMOE_TRACE(3);
 
-  // ---- full logits: sum the 8 rank partials in rank order
+  // ---- full logits: expert e is owned by rank e / EPR
   #pragma unroll 1
   for (int i = tid; i < N * E; i += kDecThreads) {
-    float s = 0.f;
-#pragma unroll
-    for (int q = 0; q < kCluster; ++q) s += cluster.map_shared_rank(part, q)[i];
-    float l = bf16r(s);
-    if (a.bias) l = bf16r(l + a.bias[i % E]);
+    const int t = i / E, e = i - t * E, r = e / EPR;
+    float l = bf16r(cluster.map_shared_rank(part, r)[t * EPR + (e - r * EPR)]);
+    if (a.bias) l = bf16r(l + a.bias[e]);
     lg[i] = l;
   }
   __syncthreads();
@@ -472,13 +526,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         const int t = g8 + 8 * hh;
-        xa[s2][hh] = (t < NT && s2 < KW) ? *reinterpret_cast<const uint2*>(xs + (size_t)t * H + 16 * k + 4 * q)
+        xa[s2][hh] = (t < NT && s2 < KW) ? *reinterpret_cast<const uint2*>(xs + (size_t)t * XP + 16 * k + 4 * q)
                                           : make_uint2(0u, 0u);
       }
     }
     __nv_bfloat16* a2t = reinterpret_cast<__nv_bfloat16*>(smem + L.a2);  // [16 tokens][8 neurons]
     if (tid < 64) reinterpret_cast<uint32_t*>(a2t)[tid] = 0u;
     __syncthreads();  // every warp holds its x fragments: the x region becomes the partials
+    PPMOE_TRACE(22);
     float* kp = reinterpret_cast<float*>(xs);
     float dacc[16][4];
 #pragma unroll
@@ -490,6 +545,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       const int nr = min(8, cnt - 8 * r);
       const uint8_t* sb = ring + (size_t)(8 * (r & 1)) * slotb;
       mbar_wait(&bars[r & 1], (uint32_t)((r >> 1) & 1), a.status);
+      if (r == 0) PPMOE_TRACE(23);
+      if (r == 1) PPMOE_TRACE(27);
       // ---- gate/up
       float d[2][4];
 #pragma unroll
@@ -522,6 +579,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
           *reinterpret_cast<float2*>(kp + ((warp * 2 + t) * NT + g8 + 8) * 8 + 2 * q) = make_float2(d[t][2], d[t][3]);
       }
       __syncthreads();
+      if (r == 0) PPMOE_TRACE(24);
       // ---- SwiGLU + gate weight per (token, neuron); warp order over the k partials
       if (tid < NT * 8) {
         const int t = tid >> 3, n = tid & 7, tl = n >> 2, i = n & 3;
@@ -541,6 +599,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         a2t[t * 8 + n] = __float2bfloat16_rn(av);
       }
       __syncthreads();
+      if (r == 0) PPMOE_TRACE(25);
       // ---- down: out[16 x 128 w..] += a2[16 x 8] * Wd[8 x ...]
       uint32_t af0, af1;
       asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
@@ -563,6 +622,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
               : "r"(af0), "r"(af1), "r"(bb[jj]));
       }
       __syncthreads();  // the round's slots and a2 are consumed
+      if (r == 0) PPMOE_TRACE(26);
       if (warp == 0 && r + 2 < rounds) issue_round(r + 2);
     }
     // CTA partial straight from the fragments: column tile j of warp w covers hidden
@@ -605,7 +665,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
         for (int v = lane; v < H / 8; v += 32) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * H + v * 8);
+          const uint4 xv = *reinterpret_cast<const uint4*>(xs + t * XP + v * 8);
           const uint4 gv = *reinterpret_cast<const uint4*>(gate + v * 8);
           const uint4 uv = *reinterpret_cast<const uint4*>(up + v * 8);
           const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
@@ -807,6 +867,10 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
                   const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
                   void* wsp, size_t ws_bytes, int pdl, cudaStream_t stream, uint32_t* status,
                   uint32_t* counters, float* cpart, size_t cpart_bytes) {
+  if (E % kCluster != 0 || H % 32 != 0) {
+    set_error("ppmoe_decode: experts (%d) must be a multiple of 8 and hidden (%d) of 32", E, H);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
   int NT = 1;
   while (NT < tokens) NT <<= 1;
   const int HCH = (H / 4 + kDecThreads - 1) / kDecThreads;
@@ -825,8 +889,9 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
     DecSmem L = dec_smem(NT, H, E, slots);
     while (slots > 2 && L.total + 1024 > (uint32_t)max_optin) L = dec_smem(NT, H, E, --slots);
     // the router slice and its group scratch alias the ring
-    const size_t need_ring = align_up((size_t)(H / kCluster) * E * 2, 128) +
-                             (size_t)max(1, kDecWarps / ((E / 2 + 31) / 32)) * NT * E * 4;
+    // router slots (E/8 padded rows) and the per-warp router partials alias the ring
+    const size_t need_ring = align_up((size_t)(E / kCluster) * (2 * H + 16), 128) +
+                             (size_t)kDecWarps * NT * 8 * ((E / kCluster + 7) / 8) * 4;
     const size_t red_ring = (size_t)NT * H * 4;
     if ((size_t)slots * dec_slot_bytes(H) < need_ring || (size_t)slots * dec_slot_bytes(H) < red_ring ||
         L.total + 1024 > (uint32_t)max_optin || slots < 2) {
@@ -865,7 +930,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
   DecodeArgs a;
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.N = tokens;
-  a.router_he = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.router_he);
+  a.router_eh = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.router_eh);
   a.experts = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.experts);
   a.H = H; a.E = E; a.G = G;
   a.tau_b = __bfloat162float(__float2bfloat16_rn(tau));

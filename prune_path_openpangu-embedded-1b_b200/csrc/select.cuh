@@ -220,7 +220,7 @@ __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPer
 // by p descending and then by expert index ascending.
 __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
                                                         float tau_b, float (&w)[kMaxExpertsPerLane],
-                                                        uint32_t* kbuf) {
+                                                        uint32_t* kbuf, bool throughput = false) {
   const int lane = threadIdx.x & 31;
   uint32_t mk = 0u;
 #pragma unroll
@@ -249,8 +249,10 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   }
   uint32_t bits = 0;
   bool done;
-  if (E <= 32) done = select_rank<1>(key, E, tau_b, bits, kbuf);
-  else if (E <= 64) done = select_rank<2>(key, E, tau_b, bits, kbuf);
+  // throughput: the bitonic network (O(E log E) work) instead of the rank count (O(E^2)
+  // work, lower latency); measured slower for 16 tokens in the fused decode, so off there.
+  if (E <= 32) done = throughput ? select_parallel<1>(key, E, tau_b, bits) : select_rank<1>(key, E, tau_b, bits, kbuf);
+  else if (E <= 64) done = throughput ? select_parallel<2>(key, E, tau_b, bits) : select_rank<2>(key, E, tau_b, bits, kbuf);
   else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
   else done = select_parallel<8>(key, E, tau_b, bits);
   if (!done) bits = select_sequential(key, E, tau_b);
