@@ -198,6 +198,46 @@ def bench_ep(P, dev, world, rank, steps, warmup, dist):
             "scaling": "strong", "recv_rows_max_over_min": rows_max / max(rows_min, 1.0)}
 
 
+def bench_decode_batch(P, dev, mods, n_tok, steps, warmup, stream):
+    """Config 2 batched decode: n_tok tokens per layer through the same 48-layer graph
+    (fused decode kernel, PDL chained).  Algorithmic bytes = union of the tokens' experts."""
+    lib, synth = P._lib, P.synth
+    xs = [synth.make_tokens(500 + l, n_tok, H).to(dev) for l in range(len(mods))]
+    outs = [torch.empty(n_tok, H, dtype=torch.bfloat16, device=dev) for _ in mods]
+    ws = mods[0].workspace(n_tok)
+    ubytes = 0
+    for l, m in enumerate(mods):
+        w = torch.empty(n_tok, E, dtype=torch.bfloat16, device=dev)
+        m.forward_decode(xs[l], weights_out=w)
+        ubytes += int((w > 0).any(0).sum()) * EXPERT_BYTES + ROUTER_BYTES + n_tok * IO_BYTES
+
+    def enqueue():
+        for l, m in enumerate(mods):
+            lib.call("ppmoe_decode", xs[l].data_ptr(), n_tok, m._packed.data_ptr(), H, E, G, TAU, None,
+                     outs[l].data_ptr(), None, None, None, ws.data_ptr(), ws.numel(), 1, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        enqueue()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        enqueue()
+    for _ in range(max(3, warmup)):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    mods[0].check_device_status()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * len(mods))
+    gbs = ubytes / len(mods) / (us * 1e-6) / 1e9
+    return {"tokens": n_tok, "us_per_layer": us, "tokens_per_s_per_layer": n_tok / (us * 1e-6),
+            "union_bytes_per_layer": ubytes / len(mods), "achieved_gbs": gbs}
+
+
 def bench_decoder(P, dev):
     """Config 4: 26-layer synthetic decoder, prompt 512 random ids, greedy 128 new tokens,
     batch 1 and 16, tau 0.70; PrunePath MoE MLP vs the dense SwiGLU MLP it replaces."""
@@ -269,6 +309,8 @@ def main():
     ap.add_argument("--no-decoder", action="store_true")
     ap.add_argument("--profile-prefill", type=int, default=0,
                     help="only run 3 prefill calls of this many tokens (for ncu captures) and exit")
+    ap.add_argument("--profile-decode", type=int, default=0,
+                    help="only run 3 decode calls of this many tokens on 8 layers (for ncu captures) and exit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
 
@@ -290,6 +332,25 @@ def main():
             m.forward_prefill(x)
         torch.cuda.synchronize()
         m.check_device_status()
+        return
+    if args.profile_decode:
+        P = importlib.import_module(PKG)
+        dev = torch.device("cuda", local)
+        ms = []
+        for l in range(8):
+            L = P.synth.make_layer(l % 4, H, E, G, router_scale=3.5)
+            m = P.TauSparseMoE(H, E * G, E, G, TAU).to(dev)
+            P.physical_reorder_for_inference(m, L.gate_w, L.up_w, L.down_w, L.router_w,
+                                             F.one_hot(L.experts_id, E).t(), TAU)
+            m.packed()
+            ms.append(m)
+        torch.cuda.synchronize()
+        x = P.synth.make_tokens(1, args.profile_decode, H).to(dev)
+        for _ in range(3):
+            for m in ms:
+                m.forward_decode(x)
+        torch.cuda.synchronize()
+        ms[0].check_device_status()
         return
     dist = None
     if world > 1:
@@ -402,6 +463,10 @@ def main():
         e2e_ms = t.item()
     e2e_us = e2e_ms * 1e3 / (e2e_steps * args.layers)
 
+    batched = {str(n): bench_decode_batch(P, dev, mods, n, max(3, args.steps // 2), args.warmup, stream)
+               for n in (4, 16)}
+    for v in batched.values():
+        v["hbm_frac"] = v["achieved_gbs"] / peaks()[0]
     pre = bench_prefill(P, dev, max(3, args.steps // 4), args.warmup) if world == 1 else None
     decr = bench_decoder(P, dev) if world == 1 and not args.no_decoder else None
     epres = bench_ep(P, dev, world, rank, max(3, args.steps // 4), args.warmup, dist) if not args.no_ep else None
@@ -427,6 +492,7 @@ def main():
                     "d2h_bytes_per_step": args.layers * H * 2,
                     "path": "TauSparseMoE.forward, eager, pinned host x/out"},
             "gpu_launches": args.steps * args.layers,
+            "decode_batched": batched,
             "prefill": pre,
             "prefill_ep": epres,
             "decoder": decr,

@@ -100,7 +100,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   return s;
 }
 
-template <int NT, int HCH>
+template <int NT, int HCH, bool CTASEL>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const DecodeArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   cg::cluster_group cluster = cg::this_cluster();
@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 
   // ---- 2. selection: a single token with E <= 64 is selected by the whole CTA, otherwise
   // one warp per token
-  if (NT == 1 && E <= 64) {
+  if constexpr (CTASEL) {  // one token, E <= 64 (chosen on the host)
     float w[kMaxExpertsPerLane];
     const uint32_t bits =
         select_one_token_cta<kDecWarps>(lg, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf));
@@ -278,24 +278,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         }
       }
     }
-  } else
+  } else {
 #pragma unroll 1
-  for (int t = warp; t < N; t += kDecWarps) {
-    float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
+    for (int t = warp; t < N; t += kDecWarps) {
+      float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-      const int e = lane + 32 * i;
-      l[i] = e < E ? lg[t * E + e] : -INFINITY;
-    }
-    if (t == 0) PPMOE_TRACE(12);
-    const uint32_t bits = select_experts_warp(l, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf) + warp * 64);
-    if (t == 0) PPMOE_TRACE(13);
+      for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+        const int e = lane + 32 * i;
+        l[i] = e < E ? lg[t * E + e] : -INFINITY;
+      }
+      if (t == 0) PPMOE_TRACE(12);
+      const uint32_t bits = select_experts_warp(l, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf) + warp * 64);
+      if (t == 0) PPMOE_TRACE(13);
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E) {
-        ws[t * E + e] = w[i];
-        if ((bits >> i) & 1u) atomicOr(&tokmask[e], 1u << t);
+      for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E) {
+          ws[t * E + e] = w[i];
+          if ((bits >> i) & 1u) atomicOr(&tokmask[e], 1u << t);
+        }
       }
     }
   }
@@ -843,8 +844,15 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 // ------------------------------------------------------------------ host side
 using KernelFn = void (*)(const DecodeArgs);
 
-static KernelFn pick_kernel(int NT, int HCH) {
-#define PPMOE_K(nt, hch) if (NT == nt && HCH == hch) return decode_fused_kernel<nt, hch>;
+static KernelFn pick_kernel(int NT, int HCH, bool ctasel) {
+  // the one-token, E <= 64 variants carry only the CTA-wide selection (smaller code)
+  if (ctasel) {
+    if (HCH == 1) return decode_fused_kernel<1, 1, true>;
+    if (HCH == 2) return decode_fused_kernel<1, 2, true>;
+    if (HCH == 3) return decode_fused_kernel<1, 3, true>;
+    return nullptr;
+  }
+#define PPMOE_K(nt, hch) if (NT == nt && HCH == hch) return decode_fused_kernel<nt, hch, false>;
   PPMOE_K(1, 1) PPMOE_K(1, 2) PPMOE_K(1, 3)
   PPMOE_K(2, 1) PPMOE_K(2, 2) PPMOE_K(2, 3)
   PPMOE_K(4, 1) PPMOE_K(4, 2) PPMOE_K(4, 3)
@@ -874,7 +882,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
   int NT = 1;
   while (NT < tokens) NT <<= 1;
   const int HCH = (H / 4 + kDecThreads - 1) / kDecThreads;
-  KernelFn fn = pick_kernel(NT, HCH);
+  KernelFn fn = pick_kernel(NT, HCH, NT == 1 && E <= 64);
   if (!fn) {
     set_error("ppmoe_decode: tokens=%d with hidden=%d is outside the decode kernel's range", tokens, H);
     return PPMOE_ERR_UNSUPPORTED;
