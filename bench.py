@@ -103,10 +103,13 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def decode_traffic():
-    """DRAM bytes per decode launch from the committed ncu capture (profiles/)."""
+def decode_traffic(bytes_per_launch):
+    """DRAM bytes per decode launch: the committed ncu capture's ratio of measured DRAM
+    traffic to algorithmic bytes (profiles/), applied to this run's mean layer."""
     p = os.path.join(ROOT, "profiles", "decode_fused_bs1.json")
-    return json.load(open(p))["dram_bytes_per_launch"] if os.path.exists(p) else None
+    if not os.path.exists(p):
+        return None
+    return json.load(open(p))["traffic_over_algorithmic"] * bytes_per_launch
 
 
 def cpu_baseline(layers, xs, seconds=10.0):
@@ -485,8 +488,8 @@ def main():
                        "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": decode_traffic(), "bytes_per_launch": step_bytes / args.layers,
-                         "kernel": "decode_fused_kernel<1,1>"},
+                         "traffic": decode_traffic(step_bytes / args.layers), "bytes_per_launch": step_bytes / args.layers,
+                         "kernel": "decode_fused_kernel<1,1,true>"},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": args.layers * H * 2,
                     "d2h_bytes_per_step": args.layers * H * 2,
