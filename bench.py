@@ -438,33 +438,49 @@ def main():
     achieved = step_bytes / args.layers / (launch_us * 1e-6) / 1e9
     peak, peak_kind = peaks()
 
-    # ---- e2e: TauSparseMoE.forward with pinned host buffers, copies inside the timed region
+    # ---- e2e: pinned host activations in, host outputs back, copies inside the timed region.
+    # (1) the C-ABI host-buffer call a plugin host makes (ppmoe_decode_host, one per layer);
+    # (2) the Python module call TauSparseMoE.forward with .to()/copy_ around it.
     xh = [x.pin_memory() for x in xs_cpu]
     oh = [torch.empty(1, H, dtype=torch.bfloat16).pin_memory() for _ in range(args.layers)]
+    xd_stage = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
+    od_stage = torch.empty(1, H, dtype=torch.bfloat16, device=dev)
     e2e_steps = max(3, min(args.steps, 10))
+    h = stream.cuda_stream
 
-    def e2e_step():
+    def e2e_abi_step():
         for l, m in enumerate(mods):
-            xd = xh[l].to(dev, non_blocking=True)
-            y = m(xd.view(1, 1, H))
-            oh[l].copy_(y.view(1, H), non_blocking=True)
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    c0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    c1.record()
-    torch.cuda.synchronize()
-    e2e_ms = c0.elapsed_time(c1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
-    e2e_us = e2e_ms * 1e3 / (e2e_steps * args.layers)
+            lib.call("ppmoe_decode_host", xh[l].data_ptr(), 1, m._packed.data_ptr(), H, E, G, TAU, None,
+                     oh[l].data_ptr(), xd_stage.data_ptr(), od_stage.data_ptr(), ws.data_ptr(), ws.numel(), h)
+
+    def e2e_module_step():
+        with torch.cuda.stream(stream):
+            for l, m in enumerate(mods):
+                xd = xh[l].to(dev, non_blocking=True)
+                y = m(xd.view(1, 1, H))
+                oh[l].copy_(y.view(1, H), non_blocking=True)
+
+    def timed(step):
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(e2e_steps):
+            step()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = c0.elapsed_time(c1)
+        if dist:
+            t = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_ms = t.item()
+        return e2e_ms * 1e3 / (e2e_steps * args.layers)
+    e2e_us = timed(e2e_abi_step)
+    e2e_module_us = timed(e2e_module_step)
+    mods[0].check_device_status()
 
     batched = {str(n): bench_decode_batch(P, dev, mods, n, max(3, args.steps // 2), args.warmup, stream)
                for n in (4, 16)}
@@ -493,7 +509,9 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": args.layers * H * 2,
                     "d2h_bytes_per_step": args.layers * H * 2,
-                    "path": "TauSparseMoE.forward, eager, pinned host x/out"},
+                    "path": "C-ABI ppmoe_decode_host per layer (pinned host x in, host out back)",
+                    "module_us_per_layer": e2e_module_us,
+                    "module_path": "TauSparseMoE.forward, eager, pinned host x .to(cuda), out copy_ to host"},
             "gpu_launches": args.steps * args.layers,
             "decode_batched": batched,
             "prefill": pre,

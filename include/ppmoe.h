@@ -104,6 +104,17 @@ PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hi
                  void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
                  void* stream);
 
+/* Host-buffer decode for callers that hold activations in (pinned) host memory, e.g. a
+ * plugin host: stream-ordered cudaMemcpyAsync of x_host [tokens][hidden] bf16 into x_dev,
+ * ppmoe_decode into out_dev (no side outputs, no programmatic dependent launch), and
+ * cudaMemcpyAsync of out_dev into out_host.  The caller synchronises the stream before reading
+ * out_host.  x_dev / out_dev: device staging buffers of tokens * hidden bf16, 16-byte aligned.
+ * Equivalent to TauSparseMoE.forward (tl:606-615) on a host tensor moved to the device and
+ * back.  Other arguments and limits as for ppmoe_decode. */
+PPMOE_API int ppmoe_decode_host(const void* x_host, int tokens, const void* packed, int hidden, int experts,
+                                int group, float tau, const float* logit_bias, void* out_host, void* x_dev,
+                                void* out_dev, void* ws, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Prefill, any token count: tcgen05 router GEMM + selection, device-side dispatch (per-expert
  * counts, 128-row tiles, token permutation; no host synchronisation), tcgen05 grouped

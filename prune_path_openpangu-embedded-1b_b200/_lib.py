@@ -48,6 +48,9 @@ SIGNATURES = {
     "ppmoe_decode": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                               _c_size_t, _c_int, _c_void_p]),
+    "ppmoe_decode_host": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
+                                   _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t,
+                                   _c_void_p]),
 }
 
 _lib = None

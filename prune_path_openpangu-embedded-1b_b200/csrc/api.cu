@@ -169,6 +169,25 @@ int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int 
                        reinterpret_cast<float*>(w8 + kWsHeader), ws_bytes - kWsHeader);
 }
 
+int ppmoe_decode_host(const void* x_host, int tokens, const void* packed, int hidden, int experts, int group,
+                      float tau, const float* logit_bias, void* out_host, void* x_dev, void* out_dev, void* ws,
+                      size_t ws_bytes, void* stream) {
+  g_err[0] = 0;
+  if (!x_host || !out_host) {
+    set_error("ppmoe_decode_host: null host pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  const size_t bytes = (size_t)tokens * (size_t)hidden * 2;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (tokens >= 1 && tokens <= PPMOE_DECODE_MAX_TOKENS && x_dev)
+    PPMOE_CHECK_CUDA(cudaMemcpyAsync(x_dev, x_host, bytes, cudaMemcpyHostToDevice, s));
+  const int rc = ppmoe_decode(x_dev, tokens, packed, hidden, experts, group, tau, logit_bias, out_dev, nullptr,
+                              nullptr, nullptr, ws, ws_bytes, 0, stream);
+  if (rc != PPMOE_OK) return rc;
+  PPMOE_CHECK_CUDA(cudaMemcpyAsync(out_host, out_dev, bytes, cudaMemcpyDeviceToHost, s));
+  return PPMOE_OK;
+}
+
 size_t ppmoe_prefill_workspace_bytes(int tokens, int hidden, int experts, int group) {
   if (check_shape("ppmoe_prefill_workspace_bytes", hidden, experts, group) || tokens < 1) return 0;
   return prefill_workspace_bytes(tokens, hidden, experts, group);

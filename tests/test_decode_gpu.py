@@ -165,3 +165,26 @@ def test_route_logits_golden_ties(golden, cuda):
         lib.call("ppmoe_route_logits", lgd.data_ptr(), n, 64, float(tau), w.data_ptr(), None,
                  torch.cuda.current_stream().cuda_stream)
         assert torch.equal(w.cpu(), d["stable"]), tau
+
+
+@pytest.mark.parametrize("batch", [1, 5])
+def test_decode_host_buffers(cuda, batch):
+    """ppmoe_decode_host (pinned host in/out, staging copies on the stream) returns exactly
+    what ppmoe_decode returns for the same activations."""
+    lib = pkg()._lib
+    synth = pkg().synth
+    L = make_layer(8, tau=0.95)
+    m = make_module(L, 0.95, cuda)
+    x = synth.make_tokens(8, batch, 1536)
+    ref = m.forward_decode(x.to(cuda)).cpu()
+    xh = x.pin_memory()
+    oh = torch.empty(batch, 1536, dtype=torch.bfloat16).pin_memory()
+    xd = torch.empty(batch, 1536, dtype=torch.bfloat16, device=cuda)
+    od = torch.empty_like(xd)
+    ws = m.workspace(batch)
+    s = torch.cuda.current_stream()
+    lib.call("ppmoe_decode_host", xh.data_ptr(), batch, m.packed().data_ptr(), 1536, 64, 96, 0.95, None,
+             oh.data_ptr(), xd.data_ptr(), od.data_ptr(), ws.data_ptr(), ws.numel(), s.cuda_stream)
+    s.synchronize()
+    m.check_device_status()
+    assert torch.equal(oh, ref)
