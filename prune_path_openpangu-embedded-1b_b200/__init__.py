@@ -6,6 +6,7 @@ directory name is not a Python identifier).  Public API:
 * ``TauSparseMoE`` -- drop-in for the reference's Triton module of the same name;
 * ``IntegratedOpenPanguMoEMLP``, ``physical_reorder_for_inference`` -- caller-side mirrors;
 * ``synth`` -- seeded synthetic layers and activations;
+* ``ingest`` -- checkpoint state_dict + cluster files -> ``TauSparseMoE`` layers;
 * ``_lib`` -- the ctypes binding of ``libppmoe.so`` (C ABI in ``include/ppmoe.h``).
 """
 from . import _lib, synth  # noqa: F401  (neither needs a GPU to import)
@@ -15,4 +16,7 @@ def __getattr__(name):
     if name in ("TauSparseMoE", "IntegratedOpenPanguMoEMLP", "physical_reorder_for_inference"):
         from . import tau_moe
         return getattr(tau_moe, name)
+    if name == "ingest":
+        import importlib
+        return importlib.import_module(__name__ + ".ingest")
     raise AttributeError(name)
