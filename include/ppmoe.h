@@ -156,6 +156,10 @@ PPMOE_API int ppmoe_prefill_experts(const void* x, int tokens, const void* packe
  * (the reference runs on one device). */
 PPMOE_API int ppmoe_ep_combine(const float* back, const int32_t* row_of, int ranks, int tokens, int hidden,
                                void* out, void* stream);
+/* Same with bf16 partial rows (back [rows][hidden] bf16): the optional reduced-traffic mode of
+ * expert-parallel prefill, whose partials are rounded to bf16 once on the expert side. */
+PPMOE_API int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int ranks, int tokens, int hidden,
+                                    void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call

@@ -41,6 +41,7 @@ SIGNATURES = {
     "ppmoe_prefill_experts": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p,
                                        _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_ep_combine": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
+    "ppmoe_ep_combine_bf16": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "ppmoe_prefill": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_decode_noalloc": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
