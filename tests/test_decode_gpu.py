@@ -188,3 +188,29 @@ def test_decode_host_buffers(cuda, batch):
     s.synchronize()
     m.check_device_status()
     assert torch.equal(oh, ref)
+
+
+@pytest.mark.parametrize("tau", [0.3, 1.0])
+@pytest.mark.parametrize("batch", [1, 2, 9])
+def test_decode_extreme_tau(cuda, batch, tau):
+    """tau 1.0 selects (nearly) every expert: one token then overflows the 24-slot
+    single-token path and runs the CUDA-core path; tau 0.3 leaves mostly the forced top-1."""
+    synth = pkg().synth
+    L = make_layer(21, tau=0.95, scale=1.0)
+    x = synth.make_tokens(21, batch, 1536)
+    m = make_module(L, tau, cuda)
+    out, lg, w = run_decode(m, x, cuda)
+    check_against_oracle(L, x, tau, out, lg, w, what=f"b{batch} tau{tau}")
+    if tau == 1.0:
+        assert int((w > 0).sum(-1).min()) > 30
+
+
+def test_decode_hidden_not_multiple_of_384(cuda):
+    """H = 1152 (H % 384 != 0 for the batched tensor-core rounds): CUDA-core multi-token path."""
+    synth = pkg().synth
+    L = make_layer(22, 1152, 32, 64, 0.7)
+    for n in (1, 6):
+        x = synth.make_tokens(22, n, 1152)
+        m = make_module(L, 0.7, cuda)
+        out, lg, w = run_decode(m, x, cuda)
+        check_against_oracle(L, x, 0.7, out, lg, w, what=f"H1152 N{n}")
