@@ -98,6 +98,26 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Distributed-shared-memory helpers: the shared::cluster address of `p` in CTA `rank`, an
+// arrival (release at cluster scope) on a barrier in another CTA of the cluster, and the
+// acquire-at-cluster-scope probe used to wait for such arrivals.
+__device__ __forceinline__ uint32_t mapa_u32(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase.  On timeout it records DEVERR_TIMEOUT in *status and
 // returns false; the caller carries on (with garbage data) so that every CTA still reaches
 // every cluster barrier and the launch ends.
@@ -108,6 +128,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (i < 8192 ? mbar_test_wait(a, parity) : mbar_try_wait(a, parity)) return true;
     if (i > 16384) __nanosleep(32);
     // once any wait of this launch has given up, stop waiting quickly everywhere else
+    if ((i & 1023u) == 1023u && status && *reinterpret_cast<volatile uint32_t*>(status)) return false;
+  }
+  if (status) atomicOr(status, DEVERR_TIMEOUT);
+  return false;
+}
+
+// mbar_wait with acquire at cluster scope (for phases completed by other CTAs' arrivals).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  const uint32_t a = smem_u32(bar);
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    if (i > 16384) __nanosleep(32);
     if ((i & 1023u) == 1023u && status && *reinterpret_cast<volatile uint32_t*>(status)) return false;
   }
   if (status) atomicOr(status, DEVERR_TIMEOUT);

@@ -72,7 +72,7 @@ __device__ __forceinline__ unsigned long long clk64() {
 
 // Shared-memory carve-out (byte offsets from a 1 KiB aligned base).
 struct DecSmem {
-  uint32_t bars, x, part, lg, w, tokmask, ulist, misc, kbuf, a2, ring, total;
+  uint32_t bars, x, part, lg, w, tokmask, ulist, misc, kbuf, a2, recv, ring, total;
 };
 
 // A neuron's gate, up and down rows are one contiguous record in its ring slot (one bulk copy);
@@ -95,6 +95,7 @@ __host__ __device__ inline DecSmem dec_smem(int NT, int H, int E, int slots) {
   s.misc = o;    o = (uint32_t)align_up(o + 64, 128);
   s.kbuf = o;    o = (uint32_t)align_up(o + (size_t)kDecWarps * 64 * 4, 128);
   s.a2 = o;      o = (uint32_t)align_up(o + (size_t)max(64 * NT, kDecWarps * 8 + 32) * 4, 1024);  // >= max(warps, slots); direct-path partials
+  s.recv = o;    o = (uint32_t)align_up(o + (NT == 1 ? (size_t)H * 4 : 0), 1024);  // one token: pushed partials
   s.ring = o;    o += (uint32_t)slots * dec_slot_bytes(H);
   s.total = o;
   return s;
@@ -129,11 +130,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
 
   PPMOE_TRACE(0);
   // ---- prologue: barriers; router slice prefetch (weights only: legal before the PDL wait)
+  // one token: the router logits and the cluster reduction are pushed into the consumer's
+  // shared memory; each pushing thread arrives (release, cluster scope) on the consumer's
+  // barrier after its own store
+  uint64_t* bar_lg = bars + a.slots + 1;   // E arrivals: 8 ranks x E/8 experts
+  uint64_t* bar_red = bars + a.slots + 2;  // 8 ranks x H/32 float4 units of this rank's slice
   if (tid == 0) {
     for (int s = 0; s <= a.slots; ++s) mbar_init(&bars[s], 1);
+    if (NT == 1) {
+      mbar_init(bar_lg, E);
+      mbar_init(bar_red, kCluster * (HS / 4));
+    }
     fence_mbar_init();
   }
   __syncthreads();
+  // every peer's barriers must be initialised before its first remote arrival: arrive here,
+  // wait just before the first push (long after, so the wait is normally free)
+  if constexpr (NT == 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // Router operands.  Rank r owns experts [r EPR, (r+1) EPR) (EPR = E / 8): their router_eh
   // rows (H contiguous bf16 each) land in padded ring slots (pitch 2H + 16 bytes) and the
   // token rows in xs at pitch XP = H + 8, so every 8-row fragment load below is
@@ -149,7 +162,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       bulk_g2s(rsl + (size_t)e * rrow, a.router_eh + (size_t)(rank * EPR + e) * H, h_bytes, bar_in,
                policy_evict_last());
   }
+  PPMOE_TRACE(28);
   if (a.pdl) pdl_wait();
+  PPMOE_TRACE(29);
   if (warp == 0)
     for (int t = lane; t < N; t += 32)
       bulk_g2s(xs + (size_t)t * XP, a.x + (size_t)t * H, h_bytes, bar_in, policy_evict_first());
@@ -198,11 +213,16 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       if (kq == 0 && j + e8 < EPR) rpart[warp * EPR + j + e8] = v;
     }
     __syncthreads();
-    for (int e = tid; e < EPR; e += kDecThreads) {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    // thread (e, r) pushes this rank's logit of expert e into CTA r's `part` (all in parallel:
+    // each release arrival waits for its own store to land)
+    for (int i = tid; i < EPR * kCluster; i += kDecThreads) {
+      const int e = i / kCluster, r = i % kCluster;
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) s += rpart[w * EPR + e];  // warp order
-      part[e] = s;
+      *cluster.map_shared_rank(part + rank * EPR + e, r) = s;
+      mbar_arrive_remote(mapa_u32(bar_lg, (uint32_t)r));
     }
   } else {
     const int NTL = (EPR + 7) >> 3;  // expert tiles
@@ -248,16 +268,25 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
   }
   PPMOE_TRACE(2);
-  cluster.sync();  // every rank's expert logits visible cluster-wide
-  PPMOE_TRACE(3);
-
-  // ---- full logits: expert e is owned by rank e / EPR
-  #pragma unroll 1
-  for (int i = tid; i < N * E; i += kDecThreads) {
-    const int t = i / E, e = i - t * E, r = e / EPR;
-    float l = bf16r(cluster.map_shared_rank(part, r)[t * EPR + (e - r * EPR)]);
-    if (a.bias) l = bf16r(l + a.bias[e]);
-    lg[i] = l;
+  if constexpr (NT == 1) {
+    mbar_wait_cluster(bar_lg, 0u, a.status);  // all E logits pushed into `part`
+    PPMOE_TRACE(3);
+    for (int e = tid; e < E; e += kDecThreads) {
+      float l = bf16r(part[e]);
+      if (a.bias) l = bf16r(l + a.bias[e]);
+      lg[e] = l;
+    }
+  } else {
+    cluster.sync();  // every rank's expert logits visible cluster-wide
+    PPMOE_TRACE(3);
+    // ---- full logits: expert e is owned by rank e / EPR
+    #pragma unroll 1
+    for (int i = tid; i < N * E; i += kDecThreads) {
+      const int t = i / E, e = i - t * E, r = e / EPR;
+      float l = bf16r(cluster.map_shared_rank(part, r)[t * EPR + (e - r * EPR)]);
+      if (a.bias) l = bf16r(l + a.bias[e]);
+      lg[i] = l;
+    }
   }
   __syncthreads();
   PPMOE_TRACE(4);
@@ -313,8 +342,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   int i0 = 0, cnt = 0;
   auto work_range = [&](int nU) {
     const int W = nU * G;
-    i0 = (int)((long long)W * blockIdx.x / gridDim.x);
-    cnt = (int)((long long)W * (blockIdx.x + 1) / gridDim.x) - i0;
+    if ((long long)W * gridDim.x < (1ll << 31)) {  // 32-bit division when the product fits
+      i0 = (int)((uint32_t)W * blockIdx.x / gridDim.x);
+      cnt = (int)((uint32_t)W * (blockIdx.x + 1) / gridDim.x) - i0;
+    } else {
+      i0 = (int)((long long)W * blockIdx.x / gridDim.x);
+      cnt = (int)((long long)W * (blockIdx.x + 1) / gridDim.x) - i0;
+    }
   };
   auto issue_neuron = [&](int n) {  // neuron n's three rows into slot n % slots
     const int gi = i0 + n;
@@ -377,12 +411,14 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   // the router slice / scratch in the ring is dead: every warp passed the barrier above
   if (fast) {
     // One bulk copy per neuron into its padded slot (pitch 6H + 32 staggers the banks of
-    // the 8-row fragment loads); tile t (neurons 4t .. 4t+3) completes on bars[t].
-    if (warp == 0 && cnt > 0) {
-      if (lane < (cnt + 3) / 4) mbar_arrive_expect_tx(&bars[lane], (uint32_t)min(4, cnt - 4 * lane) * rec_bytes);
-      __syncwarp();
+    // the 8-row fragment loads); tile t (neurons 4t .. 4t+3) completes on bars[t].  Lane 0 of
+    // warp w arms tile w and issues neurons w, w + 12, ...: copies issued by one thread are
+    // serialised (~70 cycles each), so the issue is spread over the warps.  A copy may land
+    // before its tile is armed: the phase cannot complete until the arming arrival.
+    if (lane == 0 && cnt > 0) {
+      if (warp < (cnt + 3) / 4) mbar_arrive_expect_tx(&bars[warp], (uint32_t)min(4, cnt - 4 * warp) * rec_bytes);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int n = lane; n < cnt; n += 32) {
+      for (int n = warp; n < cnt; n += kDecWarps) {
         const int gi = i0 + n, u = gi / G;
         bulk_g2s(ring + (size_t)n * slotb, a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H,
                  rec_bytes, &bars[n >> 2], pol);
@@ -741,6 +777,34 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   PPMOE_TRACE(8);
   if (a.pdl) pdl_launch_dependents();
 
+  if constexpr (NT == 1) {
+    // ---- 4a'/4b'. one token: every float4 of the CTA partial is pushed to the rank that
+    // owns its column slice (recv[source rank][HS]); the owner sums the 8 sources in rank
+    // order once all have arrived.  No cluster barrier, no shared memory read by a peer.
+    float* recv = reinterpret_cast<float*>(smem + L.recv);
+#pragma unroll
+    for (int c = 0; c < HCH; ++c) {
+      const int h4 = tid + c * kDecThreads;
+      if (h4 < H / 4) {
+        const int col = 4 * h4, owner = col / HS;
+        *reinterpret_cast<float4*>(cluster.map_shared_rank(recv + rank * HS + (col - owner * HS), owner)) =
+            make_float4(acc[c][0][0], acc[c][0][1], acc[c][0][2], acc[c][0][3]);
+        mbar_arrive_remote(mapa_u32(bar_red, (uint32_t)owner));
+      }
+    }
+    mbar_wait_cluster(bar_red, 0u, a.status);
+    PPMOE_TRACE(9);
+    #pragma unroll 1
+    for (int i = tid; i < HS / 4; i += kDecThreads) {
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int q = 0; q < kCluster; ++q) {  // rank order
+        const float4 v = *reinterpret_cast<const float4*>(recv + q * HS + 4 * i);
+        s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+      }
+      *reinterpret_cast<float4*>(a.cpart + (size_t)cid * H + rank * HS + 4 * i) = s4;
+    }
+  } else {
   // ---- 4a. CTA partial -> shared (ring is idle: every issued record has been consumed)
   float* red = reinterpret_cast<float*>(ring);
 #pragma unroll
@@ -771,6 +835,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   }
   // peers may still read this CTA's shared memory: arrive now, wait before exiting
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  }
   // ---- 4c. the last cluster to finish this column slice sums all cluster partials
   // The barrier orders every thread's partial store before thread 0's release; the
   // acquire side of the same atomic orders the last cluster's reads after all of them.
@@ -836,7 +901,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
     if (tid == 0) a.counters[rank] = 0u;  // re-arm for the next launch
   }
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if constexpr (NT != 1) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   PPMOE_TRACE(11);
   if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 30] = (unsigned long long)cnt;
 }
