@@ -85,6 +85,12 @@ PPMOE_API int ppmoe_workspace_status(void* ws, void* stream);
  * ------------------------------------------------------------------------------------- */
 PPMOE_API int ppmoe_route_logits(const void* logits, int tokens, int experts, float tau,
                        void* weights_out, uint8_t* mask_out, void* stream);
+/* Training-mode variant: also writes probs_out [N][E] bf16 = softmax(logits), the second
+ * output of softmax_thresholding(training=True) (src/MoEBlock.py:68, 93-94) that the
+ * entropy and load-balance regularisers consume (src/openpangu_moe.py:282-307).  These are
+ * exactly the probabilities the selection ranked. */
+PPMOE_API int ppmoe_route_logits_train(const void* logits, int tokens, int experts, float tau,
+                                       void* weights_out, uint8_t* mask_out, void* probs_out, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Fused decode, 1 <= tokens <= PPMOE_DECODE_MAX_TOKENS: router GEMV + selection + expert

@@ -7,6 +7,7 @@ directory name is not a Python identifier).  Public API:
 * ``IntegratedOpenPanguMoEMLP``, ``physical_reorder_for_inference`` -- caller-side mirrors;
 * ``synth`` -- seeded synthetic layers and activations;
 * ``ingest`` -- checkpoint state_dict + cluster files -> ``TauSparseMoE`` layers;
+* ``training`` -- training-mode router outputs (softmax probabilities) and auxiliary losses;
 * ``_lib`` -- the ctypes binding of ``libppmoe.so`` (C ABI in ``include/ppmoe.h``).
 """
 from . import _lib, synth  # noqa: F401  (neither needs a GPU to import)
@@ -16,7 +17,7 @@ def __getattr__(name):
     if name in ("TauSparseMoE", "IntegratedOpenPanguMoEMLP", "physical_reorder_for_inference"):
         from . import tau_moe
         return getattr(tau_moe, name)
-    if name == "ingest":
+    if name in ("ingest", "training", "ep", "decoder"):
         import importlib
-        return importlib.import_module(__name__ + ".ingest")
+        return importlib.import_module(__name__ + "." + name)
     raise AttributeError(name)

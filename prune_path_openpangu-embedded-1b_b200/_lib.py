@@ -34,6 +34,8 @@ SIGNATURES = {
     "ppmoe_workspace_status": (_c_int, [_c_void_p, _c_void_p]),
     "ppmoe_route_logits": (_c_int, [_c_void_p, _c_int, _c_int, _c_float, _c_void_p, _c_void_p,
                                     _c_void_p]),
+    "ppmoe_route_logits_train": (_c_int, [_c_void_p, _c_int, _c_int, _c_float, _c_void_p, _c_void_p,
+                                          _c_void_p, _c_void_p]),
     "ppmoe_debug_trace": (None, [_c_void_p]),
     "ppmoe_prefill_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "ppmoe_prefill_route": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,

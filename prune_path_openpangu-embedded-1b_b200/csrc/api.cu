@@ -21,7 +21,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 int pack_launch(const void*, const void*, const void*, const void*, int, int, int, void*, cudaStream_t);
-int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t);
+int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t,
+                        void* probs_out = nullptr);
 int decode_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*,
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
 
@@ -139,6 +140,21 @@ int ppmoe_route_logits(const void* logits, int tokens, int experts, float tau, v
   }
   return route_logits_launch(logits, tokens, experts, tau, nullptr, weights_out, mask_out,
                              static_cast<cudaStream_t>(stream));
+}
+
+int ppmoe_route_logits_train(const void* logits, int tokens, int experts, float tau, void* weights_out,
+                             uint8_t* mask_out, void* probs_out, void* stream) {
+  g_err[0] = 0;
+  if (tokens < 0 || experts <= 0 || experts > 256) {
+    set_error("ppmoe_route_logits_train: tokens=%d experts=%d out of range", tokens, experts);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (tokens > 0 && (!logits || !weights_out || !probs_out)) {
+    set_error("ppmoe_route_logits_train: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return route_logits_launch(logits, tokens, experts, tau, nullptr, weights_out, mask_out,
+                             static_cast<cudaStream_t>(stream), probs_out);
 }
 
 int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,

@@ -21,7 +21,8 @@
 
 namespace ppmoe {
 
-int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t);
+int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t,
+                        void* probs_out = nullptr);
 
 constexpr int kTileM = 128;
 constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
