@@ -241,6 +241,27 @@ def bench_decode_batch(P, dev, mods, n_tok, steps, warmup, stream):
             "union_bytes_per_layer": ubytes / len(mods), "achieved_gbs": gbs}
 
 
+def bench_batch64(P, dev, mods, steps, warmup):
+    """Config 2 at 64 tokens: TauSparseMoE.forward routes more than 16 tokens to the prefill
+    path (tcgen05 grouped GEMMs); 16 distinct layers, eager launches."""
+    xs = [P.synth.make_tokens(600 + l, 64, H).to(dev) for l in range(len(mods))]
+    for _ in range(max(3, warmup)):
+        for l, m in enumerate(mods):
+            m.forward_prefill(xs[l])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for l, m in enumerate(mods):
+            m.forward_prefill(xs[l])
+    e1.record()
+    torch.cuda.synchronize()
+    mods[0].check_device_status()
+    us = e0.elapsed_time(e1) * 1e3 / (steps * len(mods))
+    return {"tokens": 64, "us_per_layer": us, "tokens_per_s_per_layer": 64 / (us * 1e-6),
+            "path": "prefill kernels (more than 16 tokens)"}
+
+
 def bench_decoder(P, dev):
     """Config 4: 26-layer synthetic decoder, prompt 512 random ids, greedy 128 new tokens,
     batch 1 and 16, tau 0.70; PrunePath MoE MLP vs the dense SwiGLU MLP it replaces."""
@@ -486,6 +507,7 @@ def main():
                for n in (4, 16)}
     for v in batched.values():
         v["hbm_frac"] = v["achieved_gbs"] / peaks()[0]
+    batched["64"] = bench_batch64(P, dev, mods[:16], max(3, args.steps // 4), args.warmup)
     pre = bench_prefill(P, dev, max(3, args.steps // 4), args.warmup) if world == 1 else None
     decr = bench_decoder(P, dev) if world == 1 and not args.no_decoder else None
     epres = bench_ep(P, dev, world, rank, max(3, args.steps // 4), args.warmup, dist) if not args.no_ep else None
