@@ -469,10 +469,16 @@ def main():
     e2e_steps = max(3, min(args.steps, 10))
     h = stream.cuda_stream
 
+    # a plugin host binds the entry point once and keeps its buffer addresses
+    decode_host = lib.load().ppmoe_decode_host
+    bound = [(xh[l].data_ptr(), m._packed.data_ptr(), oh[l].data_ptr()) for l, m in enumerate(mods)]
+    xd_p, od_p, ws_p, ws_n = xd_stage.data_ptr(), od_stage.data_ptr(), ws.data_ptr(), ws.numel()
+
     def e2e_abi_step():
-        for l, m in enumerate(mods):
-            lib.call("ppmoe_decode_host", xh[l].data_ptr(), 1, m._packed.data_ptr(), H, E, G, TAU, None,
-                     oh[l].data_ptr(), xd_stage.data_ptr(), od_stage.data_ptr(), ws.data_ptr(), ws.numel(), h)
+        for xp, pp, op in bound:
+            rc = decode_host(xp, 1, pp, H, E, G, TAU, None, op, xd_p, od_p, ws_p, ws_n, h)
+            if rc:
+                raise RuntimeError(f"ppmoe_decode_host -> {rc}: {lib.load().ppmoe_last_error().decode()}")
 
     def e2e_module_step():
         with torch.cuda.stream(stream):
@@ -531,7 +537,7 @@ def main():
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_us, "unit": "us/layer", "h2d_bytes_per_step": args.layers * H * 2,
                     "d2h_bytes_per_step": args.layers * H * 2,
-                    "path": "C-ABI ppmoe_decode_host per layer (pinned host x in, host out back)",
+                    "path": "C-ABI ppmoe_decode_host per layer (pinned host x in, host out back; entry point bound once)",
                     "module_us_per_layer": e2e_module_us,
                     "module_path": "TauSparseMoE.forward, eager, pinned host x .to(cuda), out copy_ to host"},
             "gpu_launches": args.steps * args.layers,

@@ -110,11 +110,15 @@ PPMOE_API int ppmoe_decode(const void* x, int tokens, const void* packed, int hi
                  void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl,
                  void* stream);
 
-/* Host-buffer decode for callers that hold activations in (pinned) host memory, e.g. a
- * plugin host: stream-ordered cudaMemcpyAsync of x_host [tokens][hidden] bf16 into x_dev,
- * ppmoe_decode into out_dev (no side outputs, no programmatic dependent launch), and
- * cudaMemcpyAsync of out_dev into out_host.  The caller synchronises the stream before reading
- * out_host.  x_dev / out_dev: device staging buffers of tokens * hidden bf16, 16-byte aligned.
+/* Host-buffer decode for callers that hold activations in host memory, e.g. a plugin host:
+ * x_host [tokens][hidden] bf16 is staged into x_dev (pinned, mapped host memory: by a
+ * one-CTA kernel chained to the decode with programmatic dependent launch, so the transfer
+ * overlaps the previous call's decode; pageable memory: by a stream-ordered
+ * cudaMemcpyAsync), then the fused decode.  When out_host is pinned and mapped into the device address space (cudaHostAlloc /
+ * torch pin_memory on a UVA system) the kernel writes the bf16 output into it directly;
+ * otherwise into out_dev followed by a cudaMemcpyAsync into out_host.  The caller
+ * synchronises the stream before reading out_host.  x_dev / out_dev: device staging buffers
+ * of tokens * hidden bf16, 16-byte aligned (out_dev unused when out_host is pinned).
  * Equivalent to TauSparseMoE.forward (tl:606-615) on a host tensor moved to the device and
  * back.  Other arguments and limits as for ppmoe_decode. */
 PPMOE_API int ppmoe_decode_host(const void* x_host, int tokens, const void* packed, int hidden, int experts,

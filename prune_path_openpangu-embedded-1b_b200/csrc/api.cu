@@ -24,7 +24,7 @@ int pack_launch(const void*, const void*, const void*, const void*, int, int, in
 int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t,
                         void* probs_out = nullptr);
 int decode_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*,
-                  int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
+                  int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 void decode_set_trace(void*);
 size_t prefill_workspace_bytes(long long, int, int, int);
@@ -157,32 +157,78 @@ int ppmoe_route_logits_train(const void* logits, int tokens, int experts, float 
                              static_cast<cudaStream_t>(stream), probs_out);
 }
 
-int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
-                 const float* logit_bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
-                 void* ws, size_t ws_bytes, int pdl, void* stream) {
-  g_err[0] = 0;
-  if (int rc = check_shape("ppmoe_decode", hidden, experts, group)) return rc;
+static int decode_checked(const char* fn, const void* x, int tokens, const void* packed, int hidden, int experts,
+                          int group, float tau, const float* logit_bias, void* out, void* logits_out,
+                          void* weights_out, int64_t* counts, void* ws, size_t ws_bytes, int pdl, void* stream,
+                          int x_host) {
+  if (int rc = check_shape(fn, hidden, experts, group)) return rc;
   if (tokens < 1 || tokens > PPMOE_DECODE_MAX_TOKENS) {
-    set_error("ppmoe_decode: tokens=%d must be in [1, %d]", tokens, PPMOE_DECODE_MAX_TOKENS);
+    set_error("%s: tokens=%d must be in [1, %d]", fn, tokens, PPMOE_DECODE_MAX_TOKENS);
     return PPMOE_ERR_UNSUPPORTED;
   }
   if (!x || !packed || !out || !ws) {
-    set_error("ppmoe_decode: null pointer");
+    set_error("%s: null pointer", fn);
     return PPMOE_ERR_INVALID_ARG;
   }
   if (!aligned(x, 16) || !aligned(out, 16) || !aligned(packed, 1024) || !aligned(ws, 256)) {
-    set_error("ppmoe_decode: x/out must be 16-byte, packed 1024-byte, ws 256-byte aligned");
+    set_error("%s: x/out must be 16-byte, packed 1024-byte, ws 256-byte aligned", fn);
     return PPMOE_ERR_INVALID_ARG;
   }
   if (ws_bytes < kWsHeader) {
-    set_error("ppmoe_decode: workspace too small");
+    set_error("%s: workspace too small", fn);
     return PPMOE_ERR_WORKSPACE;
   }
   uint8_t* w8 = static_cast<uint8_t*>(ws);
   return decode_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, out, logits_out, weights_out,
                        counts, ws, ws_bytes, pdl, static_cast<cudaStream_t>(stream),
                        reinterpret_cast<uint32_t*>(w8), reinterpret_cast<uint32_t*>(w8 + kWsCounters),
-                       reinterpret_cast<float*>(w8 + kWsHeader), ws_bytes - kWsHeader);
+                       reinterpret_cast<float*>(w8 + kWsHeader), ws_bytes - kWsHeader, x_host);
+}
+
+int ppmoe_decode(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
+                 const float* logit_bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
+                 void* ws, size_t ws_bytes, int pdl, void* stream) {
+  g_err[0] = 0;
+  return decode_checked("ppmoe_decode", x, tokens, packed, hidden, experts, group, tau, logit_bias, out, logits_out,
+                        weights_out, counts, ws, ws_bytes, pdl, stream, 0);
+}
+
+// Token rows from pinned host memory into the staging buffer, one CTA, chained by
+// programmatic dependent launch between the previous decode and the next one: it lets the
+// next decode launch at once (its prologue loads only weights), copies while the previous
+// decode is still finishing, and exits only after that decode has completed, so the next
+// decode's griddepcontrol.wait also covers the previous decode (which used the same
+// workspace).  Overwriting x_dev early is safe: this grid starts only after every CTA of the
+// previous decode has signalled its dependents, which each does long after its rows landed.
+__global__ void x_stage_kernel(const uint4* src_host, uint4* __restrict__ dst, int n16) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src_host[i];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+static int launch_x_stage(const void* src_host, void* dst, size_t bytes, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  PPMOE_CHECK_CUDA(cudaLaunchKernelEx(&cfg, x_stage_kernel, static_cast<const uint4*>(src_host),
+                                      static_cast<uint4*>(dst), (int)(bytes / 16)));
+  return PPMOE_OK;
+}
+
+// Device address of pinned, mapped host memory, or null (pageable or unregistered memory).
+static void* mapped_host(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();  // clear the error of an unregistered pointer
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
 }
 
 int ppmoe_decode_host(const void* x_host, int tokens, const void* packed, int hidden, int experts, int group,
@@ -193,13 +239,26 @@ int ppmoe_decode_host(const void* x_host, int tokens, const void* packed, int hi
     set_error("ppmoe_decode_host: null host pointer");
     return PPMOE_ERR_INVALID_ARG;
   }
+  // Token rows: pinned, mapped host memory is staged by a one-CTA kernel chained with
+  // programmatic dependent launch (the copy overlaps the previous decode; reading host memory
+  // from every CTA of the decode itself means thousands of small reads over the host link,
+  // measured ~4x slower); pageable memory by a stream-ordered copy.  The output is small and
+  // written by a few CTAs: into pinned, mapped host memory directly when out_host allows it
+  // (no device-to-host copy operation), else via out_dev.
   const size_t bytes = (size_t)tokens * (size_t)hidden * 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (tokens >= 1 && tokens <= PPMOE_DECODE_MAX_TOKENS && x_dev)
-    PPMOE_CHECK_CUDA(cudaMemcpyAsync(x_dev, x_host, bytes, cudaMemcpyHostToDevice, s));
-  const int rc = ppmoe_decode(x_dev, tokens, packed, hidden, experts, group, tau, logit_bias, out_dev, nullptr,
-                              nullptr, nullptr, ws, ws_bytes, 0, stream);
-  if (rc != PPMOE_OK) return rc;
+  void* xm = mapped_host(x_host);
+  const bool ok_tokens = tokens >= 1 && tokens <= PPMOE_DECODE_MAX_TOKENS && x_dev;
+  if (ok_tokens && xm && aligned(xm, 16) && aligned(x_dev, 16)) {
+    if (int rc = launch_x_stage(xm, x_dev, bytes, s)) return rc;
+  } else {
+    xm = nullptr;
+    if (ok_tokens) PPMOE_CHECK_CUDA(cudaMemcpyAsync(x_dev, x_host, bytes, cudaMemcpyHostToDevice, s));
+  }
+  void* om = mapped_host(out_host);
+  const int rc = decode_checked("ppmoe_decode_host", x_dev, tokens, packed, hidden, experts, group, tau, logit_bias,
+                                om ? om : out_dev, nullptr, nullptr, nullptr, ws, ws_bytes, xm ? 1 : 0, stream, 0);
+  if (rc != PPMOE_OK || om) return rc;
   PPMOE_CHECK_CUDA(cudaMemcpyAsync(out_host, out_dev, bytes, cudaMemcpyDeviceToHost, s));
   return PPMOE_OK;
 }

@@ -59,6 +59,7 @@ struct DecodeArgs {
   uint32_t* status;
   int slots;           // ring depth
   int pdl;
+  int x_host;  // x is pinned, device-mapped host memory: plain loads instead of a bulk copy
   unsigned long long* trace;  // optional per-CTA phase timestamps [grid][32] (diagnostics)
 };
 
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   const uint32_t h_bytes = 2u * (uint32_t)H;
   uint8_t* rsl = ring;  // router slots alias the ring
   if (warp == 0) {
-    if (lane == 0) mbar_arrive_expect_tx(bar_in, (uint32_t)(EPR + N) * h_bytes);
+    if (lane == 0) mbar_arrive_expect_tx(bar_in, (uint32_t)(EPR + (a.x_host ? 0 : N)) * h_bytes);
     __syncwarp();
     for (int e = lane; e < EPR; e += 32)
       bulk_g2s(rsl + (size_t)e * rrow, a.router_eh + (size_t)(rank * EPR + e) * H, h_bytes, bar_in,
@@ -165,15 +166,26 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   PPMOE_TRACE(28);
   if (a.pdl) pdl_wait();
   PPMOE_TRACE(29);
-  if (warp == 0)
+  if (a.x_host) {
+    // token rows straight from pinned host memory (no bulk copy from system memory): 16-byte
+    // loads, ordered before their use by the barrier after the router-row wait below
+    const int per = H / 8;
+    #pragma unroll 1
+    for (int i = tid; i < N * per; i += kDecThreads) {
+      const int t = i / per, c = i - t * per;
+      reinterpret_cast<uint4*>(xs + (size_t)t * XP)[c] = reinterpret_cast<const uint4*>(a.x + (size_t)t * H)[c];
+    }
+  } else if (warp == 0) {
     for (int t = lane; t < N; t += 32)
       bulk_g2s(xs + (size_t)t * XP, a.x + (size_t)t * H, h_bytes, bar_in, policy_evict_first());
+  }
   // zero-fill padded token rows so that their (ignored) logits stay finite
   #pragma unroll 1
   for (int i = tid; i < (NT - N) * XP; i += kDecThreads) xs[(size_t)N * XP + i] = __float2bfloat16_rn(0.f);
   #pragma unroll 1
   for (int i = tid; i < E; i += kDecThreads) tokmask[i] = 0u;
   mbar_wait(bar_in, 0, a.status);
+  if (a.x_host) __syncthreads();
   PPMOE_TRACE(1);
 
   // ---- 1. this rank's experts' logits on the tensor cores: D[16 tokens x 8 experts] per
@@ -939,7 +951,7 @@ void decode_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(bu
 int decode_launch(const void* x, int tokens, const void* packed, int H, int E, int G, float tau,
                   const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
                   void* wsp, size_t ws_bytes, int pdl, cudaStream_t stream, uint32_t* status,
-                  uint32_t* counters, float* cpart, size_t cpart_bytes) {
+                  uint32_t* counters, float* cpart, size_t cpart_bytes, int x_host) {
   if (E % kCluster != 0 || H % 32 != 0) {
     set_error("ppmoe_decode: experts (%d) must be a multiple of 8 and hidden (%d) of 32", E, H);
     return PPMOE_ERR_UNSUPPORTED;
@@ -1017,6 +1029,7 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
   a.status = status;
   a.slots = C.slots;
   a.pdl = pdl;
+  a.x_host = x_host;
   a.trace = g_trace;
 
   cudaLaunchConfig_t cfg = {};

@@ -11,7 +11,7 @@
 namespace ppmoe {
 
 int decode_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*,
-                  int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t);
+                  int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 // Scratch limit: tokens * hidden <= 8192 (e.g. 5 tokens at hidden 1536, 4 at 2048, 16 at
 // 512) for up to 32 clusters of the decode grid: 32 * 8192 * 4 bytes of partials plus a

@@ -167,18 +167,22 @@ def test_route_logits_golden_ties(golden, cuda):
         assert torch.equal(w.cpu(), d["stable"]), tau
 
 
+@pytest.mark.parametrize("pinned", [True, False])
 @pytest.mark.parametrize("batch", [1, 5])
-def test_decode_host_buffers(cuda, batch):
-    """ppmoe_decode_host (pinned host in/out, staging copies on the stream) returns exactly
-    what ppmoe_decode returns for the same activations."""
+def test_decode_host_buffers(cuda, batch, pinned):
+    """ppmoe_decode_host returns exactly what ppmoe_decode returns for the same activations:
+    pinned host buffers (the kernel reads and writes them over the host link) and pageable
+    ones (staging copies on the stream)."""
     lib = pkg()._lib
     synth = pkg().synth
     L = make_layer(8, tau=0.95)
     m = make_module(L, 0.95, cuda)
     x = synth.make_tokens(8, batch, 1536)
     ref = m.forward_decode(x.to(cuda)).cpu()
-    xh = x.pin_memory()
-    oh = torch.empty(batch, 1536, dtype=torch.bfloat16).pin_memory()
+    xh = x.pin_memory() if pinned else x.clone()
+    oh = torch.empty(batch, 1536, dtype=torch.bfloat16)
+    if pinned:
+        oh = oh.pin_memory()
     xd = torch.empty(batch, 1536, dtype=torch.bfloat16, device=cuda)
     od = torch.empty_like(xd)
     ws = m.workspace(batch)
