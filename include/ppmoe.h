@@ -55,8 +55,8 @@ PPMOE_API const char* ppmoe_last_error(void);
  * (src/openpangu_moe.py:212-256) mounts on TauSparseMoE's buffers W_gate [H,I],
  * W_up [H,I], W_down [I,H], router [H,E] (tl:483-486): this call reads exactly those
  * buffers and writes one packed, 1 KiB-aligned blob:
- *   router_he [H][E] | router_eh [E][H] | experts [E][G][3][H] (gate row, up row, down row
- *   of each neuron, contiguous) | down_t [E][H][G]
+ *   router_eh [E][H] | experts [E][G][3][H] (gate row, up row, down row of each neuron,
+ *   contiguous) | down_t [E][H][G]
  * ------------------------------------------------------------------------------------- */
 PPMOE_API size_t ppmoe_packed_bytes(int hidden, int experts, int group);
 PPMOE_API int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_down, const void* router,

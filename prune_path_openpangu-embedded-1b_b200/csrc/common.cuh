@@ -35,7 +35,7 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 
 // ------------------------------------------------------------------ layout of the blob
 struct PackedLayout {
-  size_t router_he, router_eh, experts, down_t, total;
+  size_t router_eh, experts, down_t, total;
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -43,7 +43,6 @@ __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a -
 __host__ __device__ inline PackedLayout packed_layout(int H, int E, int G) {
   PackedLayout L;
   size_t off = 0;
-  L.router_he = off; off = align_up(off + (size_t)H * E * 2, 1024);
   L.router_eh = off; off = align_up(off + (size_t)H * E * 2, 1024);
   L.experts = off;   off = align_up(off + (size_t)E * G * 3 * H * 2, 1024);
   L.down_t = off;    off = align_up(off + (size_t)E * G * H * 2, 1024);

@@ -1,8 +1,8 @@
 // Packing pass: the reference-layout buffers that physical_reorder_for_inference mounts on
 // TauSparseMoE (src/openpangu_moe.py:234-243: W_gate [H,I], W_up [H,I], W_down [I,H],
 // router [H,E], neurons already grouped by expert) -> one packed blob (common.cuh):
-//   router_he [H][E]   copy of router (decode K-split: a row slice is contiguous)
-//   router_eh [E][H]   transpose (K-major operand for the prefill router GEMM)
+//   router_eh [E][H]   transpose (one expert's router row contiguous: the decode router's
+//                      per-rank rows and the K-major operand of the prefill router GEMM)
 //   experts [E][G][3][H] per neuron n = e*G+j: W_gate[:,n] | W_up[:,n] | W_down[n,:]
 //                      (one contiguous 3*H*2-byte record: what a decode CTA streams)
 //   down_t [E][H][G]   per expert, W_down[e*G:(e+1)*G, :] transposed (K-major operand of
@@ -46,7 +46,6 @@ int pack_launch(const void* Wg, const void* Wu, const void* Wd, const void* R, i
   uint8_t* p = static_cast<uint8_t*>(packed);
   const long long I = (long long)E * G;
   int rc;
-  PPMOE_CHECK_CUDA(cudaMemcpyAsync(p + L.router_he, R, (size_t)H * E * 2, cudaMemcpyDeviceToDevice, st));
   if ((rc = transpose(R, p + L.router_eh, H, E, E, H, 1, 0, 0, st))) return rc;
   uint16_t* ex = reinterpret_cast<uint16_t*>(p + L.experts);
   if ((rc = transpose(Wg, ex, H, (int)I, I, 3LL * H, 1, 0, 0, st))) return rc;
