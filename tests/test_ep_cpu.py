@@ -1,4 +1,4 @@
-"""Expert-parallel prefill host logic on CPU ranks (gloo, world size 2): dispatch plan, count
+"""Expert-parallel prefill host logic on CPU ranks (gloo, world size 2 and 4): dispatch plan, count
 and payload exchange, partial return, deterministic combine.  Kernels are replaced by CPU
 stand-ins built from the oracle; the GPU path is covered by tests/test_ep_gpu.py."""
 import datetime
@@ -44,7 +44,8 @@ def _worker(rank, world, port, q, mode):
         ep = import_module(P.__name__ + ".ep")
         L = P.synth.make_layer(8, 128, 16, 32, router_scale=1.75)
         x = P.synth.make_tokens(8, 96, 128)
-        shard = x[rank * 48:(rank + 1) * 48]
+        n = 96 // world
+        shard = x[rank * n:(rank + 1) * n]
         # with injected kernels the layer only needs its shapes (no device weights)
         m = ep.ExpertParallelMoE.__new__(ep.ExpertParallelMoE)
         m.group, m.world, m.rank = None, world, rank
@@ -82,9 +83,10 @@ def _run(mode, world=2):
     return res
 
 
-def test_ep_two_ranks_matches_oracle():
-    res = _run("ok")
-    assert res[0][0] == "ok" and res[1][0] == "ok", res
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_ranks_match_oracle(world):
+    res = _run("ok", world)
+    assert all(res[r][0] == "ok" for r in range(world)), res
     y = res[0][1]
     P = pkg()
     L = P.synth.make_layer(8, 128, 16, 32, router_scale=1.75)
