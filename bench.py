@@ -1,4 +1,4 @@
-"""Benchmark: PrunePath MoE-MLP decode latency per layer at batch 1.
+"""Benchmark: PrunePath MoE-MLP decode latency per layer at batch 1 (H=1536, E=64, G=96, tau 0.95).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 

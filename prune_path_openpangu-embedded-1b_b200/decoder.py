@@ -1,4 +1,4 @@
-"""Synthetic PrunePath decoder for end-to-end decode measurement.
+"""Synthetic PrunePath decoder for end-to-end decode measurement (26 layers, prompt 512, 128 new tokens).
 
 26 pre-norm decoder layers, hidden 1536, 12 attention heads x 128 (multi-head attention: the
 openPangu KV-head count is not given in the reference, which loads the HF model remotely,

@@ -1,5 +1,5 @@
 """GPU parity of the fused decode kernel and the selection kernel against the CPU oracle
-and the reference's golden vectors (BASELINE configs 1 and 2: batch 1..16)."""
+and the reference's golden vectors (decode at batch 1..16)."""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -56,7 +56,7 @@ def test_decode_golden_cases(golden, cuda):
 @pytest.mark.parametrize("tau", [0.70, 0.95])
 @pytest.mark.parametrize("batch", [1, 4, 16])
 def test_decode_sweep(cuda, batch, tau):
-    """BASELINE config 2 (batch 1/4/16 x tau, seeds 0-3) at the full layer shape."""
+    """Batched decode (batch 1/4/16 x tau, seeds 0-3) at the full layer shape."""
     synth = pkg().synth
     stats = []
     for seed in range(4):

@@ -1,4 +1,4 @@
-"""GPU parity of the tcgen05 prefill path (BASELINE configs 2 at batch 64 and 3) against the
+"""GPU parity of the tcgen05 prefill path (batch 64 and 8 x 2048 tokens) against the
 CPU oracle, plus consistency with the fused decode kernel."""
 import pytest
 import torch
@@ -40,7 +40,7 @@ def test_prefill_vs_oracle(cuda, shape):
 
 
 def test_prefill_config3_full_size(cuda):
-    """8 x 2048 tokens, tau 0.70, against the teacher-forced oracle."""
+    """Prefill of 8 x 2048 tokens, tau 0.70, against the teacher-forced oracle."""
     H, E, G, tau = 1536, 64, 96, 0.70
     L = make_layer(3, H, E, G, tau)
     x = pkg().synth.make_tokens(3, 16384, H)
