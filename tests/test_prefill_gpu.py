@@ -75,3 +75,5 @@ def test_prefill_zipf_bias(cuda):
     x = pkg().synth.make_tokens(4, 700, H)
     out, lg, w = run_prefill(m, x, cuda, bias=b.to(cuda))
     check(L, x, tau, out, lg, w, bias=b, what="zipf")
+    out2, lg2, w2 = run_prefill(m, x, cuda, bias=b.to(cuda))  # fixed-order sums: bit-reproducible
+    assert torch.equal(out2, out) and torch.equal(w2, w) and torch.equal(lg2, lg)
