@@ -133,6 +133,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// mbar_wait for waits that usually last long (pipeline stages, accumulator hand-offs): polls
+// with the suspending try_wait from the first probe, so that waiting warps do not take issue
+// slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_wait_parked(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  const uint32_t a = smem_u32(bar);
+#pragma unroll 1
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(a, parity)) return true;
+    if (i > 16384) __nanosleep(32);
+    if ((i & 1023u) == 1023u && status && *reinterpret_cast<volatile uint32_t*>(status)) return false;
+  }
+  if (status) atomicOr(status, DEVERR_TIMEOUT);
+  return false;
+}
+
 // mbar_wait with acquire at cluster scope (for phases completed by other CTAs' arrivals).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t* status) {
   const uint32_t a = smem_u32(bar);

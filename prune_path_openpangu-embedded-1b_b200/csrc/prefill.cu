@@ -8,11 +8,12 @@
 //                                             the worst-case-sized workspace removes the host
 //                                             sync and the 512-tile-per-expert cap (tl:176)
 //   moe_dispatch_kernel (tl:217-266)        -> scatter_kernel (token order within expert)
-//   moe_fused_expert_kernel (tl:271-328)    -> gu_gemm_kernel (gathered token rows x the
-//                                             expert's interleaved gate/up rows, SwiGLU and
-//                                             gate weight in the epilogue -> a2 rows) +
-//                                             down_gemm_kernel (a2 x down_t, one fp32 row per
-//                                             pair) + pair_combine_kernel (per token, its rows in
+//   moe_fused_expert_kernel (tl:271-328)    -> gu_gemm_pair_kernel (gathered token rows of
+//                                             two 128-row tiles x the expert's interleaved
+//                                             gate/up rows, SwiGLU and gate weight in the
+//                                             epilogue -> a2 rows) + down_gemm_kernel (a2 x
+//                                             down_t, one 24-bit-float row per pair) +
+//                                             pair_combine_kernel (per token, its rows in
 //                                             expert order)
 // Numerics follow the reference's bf16 rounding points; the per-token combine over experts
 // accumulates in fp32 and rounds once (the reference Triton kernel adds bf16 atomics).
@@ -28,8 +29,8 @@ constexpr int kTileM = 128;
 constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
 
 struct PrefillWs {
-  size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, pair_token, pair_w,
-      a2, ypart, tok_pairs, tok_k, status, total;
+  size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, unit_tile, pair_token,
+      pair_w, a2, ypart, tok_pairs, tok_k, status, total;
   long long max_pairs, max_tiles;
   int nblocks;
 };
@@ -51,10 +52,11 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   w.ntiles = take(16);
   w.tile_expert = take((size_t)w.max_tiles * 4);
   w.tile_row0 = take((size_t)w.max_tiles * 4);
+  w.unit_tile = take((size_t)w.max_tiles * 4);
   w.pair_token = take((size_t)w.max_pairs * 4);
   w.pair_w = take((size_t)w.max_pairs * 4);
   w.a2 = take((size_t)w.max_pairs * G * 2);
-  w.ypart = take((size_t)w.max_pairs * H * 4);  // fp32 down-projection row of every pair
+  w.ypart = take((size_t)w.max_pairs * H * 3);  // 24-bit down-projection row of every pair (2 planes)
   w.tok_pairs = take((size_t)N * E * 4);        // per token: its pairs in expert order
   w.tok_k = take((size_t)N * 4);
   w.total = o;
@@ -100,7 +102,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
   if (warp == 4 && lane == 0) {  // TMA producer
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % a.stages;
-      mbar_wait(&empty[s], ((kb / a.stages) & 1) ^ 1, a.status);
+      mbar_wait_parked(&empty[s], ((kb / a.stages) & 1) ^ 1, a.status);
       uint8_t* st = smem + s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_2d(st, &mapX, kb * kBK, tile * kTileM, &full[s]);
@@ -110,7 +112,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.EP);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % a.stages;
-      mbar_wait(&full[s], (kb / a.stages) & 1, a.status);
+      mbar_wait_parked(&full[s], (kb / a.stages) & 1, a.status);
       tc_fence_after();
       const uint32_t sa = smem_u32(smem + s * stage_bytes);
       const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
@@ -120,7 +122,7 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
     }
     umma_commit(tfull);
   } else if (warp < 4) {  // epilogue: row = token
-    mbar_wait(tfull, 0, a.status);
+    mbar_wait_parked(tfull, 0, a.status);
     tc_fence_after();
     const int t = tile * kTileM + warp * 32 + lane;
     for (int c0 = 0; c0 < a.EP; c0 += 32) {
@@ -176,9 +178,11 @@ __global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int N, int E, 
 // padding rows, activation counts.
 __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E, int* __restrict__ blockoff,
                             int* __restrict__ count, int* __restrict__ exp_off, int* __restrict__ ntiles,
-                            int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ pair_token,
-                            float* __restrict__ pair_w, long long* __restrict__ act_counts) {
+                            int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ unit_tile,
+                            int* __restrict__ pair_token, float* __restrict__ pair_w,
+                            long long* __restrict__ act_counts) {
   __shared__ int off_s[257];
+  __shared__ int uoff_s[257];
   __shared__ int cnt_s[256];
   const int e = threadIdx.x;
   int run = 0;
@@ -200,13 +204,17 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
   }
   __syncthreads();
   if (e == 0) {
-    int o = 0;
+    int o = 0, u = 0;
     for (int q = 0; q < E; ++q) {
       off_s[q] = o;
-      o += (cnt_s[q] + kTileM - 1) / kTileM * kTileM;
+      uoff_s[q] = u;
+      const int t = (cnt_s[q] + kTileM - 1) / kTileM;
+      o += t * kTileM;
+      u += (t + 1) / 2;
     }
     off_s[E] = o;
-    *ntiles = o / kTileM;
+    ntiles[0] = o / kTileM;
+    ntiles[1] = u;
   }
   __syncthreads();
   if (e < E) {
@@ -217,6 +225,9 @@ __global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E
       tile_expert[o / kTileM + i] = e;
       tile_row0[o / kTileM + i] = o + i * kTileM;
     }
+    // gate/up work units: consecutive tile pairs of one expert (first tile * 2 + has-second)
+    const int t = padded / kTileM;
+    for (int i = 0; i < t; i += 2) unit_tile[uoff_s[e] + i / 2] = (o / kTileM + i) * 2 + (i + 1 < t);
   }
   // padding rows of every expert's last tile, spread over the whole block
   for (int q = 0; q < E; ++q)
@@ -286,62 +297,78 @@ struct GUArgs {
   const float* pair_w;
   __nv_bfloat16* a2;  // [pairs][G]
   uint32_t* status;
-  int stages;  // pipeline depth (5, or 4 when 2G = 256 rows per B stage)
+  int stages;  // pipeline depth (set from the shared-memory budget)
 };
 
 constexpr int kGUMaxStages = 5;  // cp.async groups kept in flight per producer thread
 
-__global__ void __launch_bounds__(320, 1)
-gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
+// Gate/up over tile PAIRS: two 128-row tiles of one expert share every B (weight) stage, so
+// each expert's gate/up rows are read from L2 once per 256 pair rows instead of once per 128.
+// Per 64-wide k-block: two 128 x 2G x 16 MMAs per k step (accumulators at TMEM columns 0 and
+// 256).  Warps 0-7 are the epilogue (warp w: tile w / 4, TMEM lane quarter w % 4), warps
+// 8-15 gather the 256 token rows with cp.async, warp 16 allocates TMEM and issues the MMAs.
+// The one accumulator pair is not double-buffered (2 x 2G columns fill TMEM's 512), so a
+// unit's epilogue runs before the next unit's first MMA.
+struct GUPairArgs {
+  GUArgs g;
+  const int* unit_tile;  // per unit: first tile * 2 + (1 if the unit has a second tile)
+};
+
+__global__ void __launch_bounds__(544, 1)
+gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs pa) {
+  const GUArgs& a = pa.g;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int S = a.stages, LAG = S - 2;  // cp.async groups kept in flight per producer thread
-  const int NB = 2 * a.G;  // interleaved gate/up rows = MMA N
+  const int S = a.stages, LAG = S - 2;
+  const int NB = 2 * a.G;
   const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)NB * 128;
-  const uint32_t stage_bytes = a_bytes + b_bytes;
+  const uint32_t stage_bytes = 2 * a_bytes + b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
   const int KB = a.H / kBK;
-  const int ntiles = *a.ntiles;
+  const int nunits = a.ntiles[1];
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 129); mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 257); mbar_init(&empty[s], 1); }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 256);
     fence_mbar_init();
   }
-  if (warp == 8) tmem_alloc(tmem_slot, 512);
+  if (warp == 16) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 4 && warp < 8) {  // producers: one gathered token row each; B via TMA
-    const int pr = tid - 128;
+  if (warp >= 8 && warp < 16) {  // producers: one gathered token row each; B via TMA
+    const int pr = tid - 256, h = pr >> 7, row = pr & 127;
+    const uint32_t aoff = h * a_bytes;
     int it = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int e = a.tile_expert[tile];
-      int tok = a.pair_token[a.tile_row0[tile] + pr];
-      // padding rows load nothing: their stale shared-memory contents only reach their own
-      // (discarded) accumulator rows, and skipping them avoids every CTA hammering one row
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      const int ut = pa.unit_tile[u], t0 = ut >> 1;
+      const int e = a.tile_expert[t0];
+      // padding rows and the absent second tile load nothing: their stale shared-memory rows
+      // only reach accumulator rows that the epilogue discards
+      const int tok = (h == 0 || (ut & 1)) ? a.pair_token[a.tile_row0[t0 + h] + row] : -1;
       const bool real = tok >= 0;
       const __nv_bfloat16* src = a.x + (size_t)(real ? tok : 0) * a.H;
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
-        mbar_wait(&empty[s], ((it / S) & 1) ^ 1, a.status);
-        uint8_t* st = smem + s * stage_bytes;
+        mbar_wait_parked(&empty[s], ((it / S) & 1) ^ 1, a.status);
+        uint8_t* st = smem + s * stage_bytes + aoff;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          if (real) cp_async16(st + sw128_offset(pr, c), src + kb * kBK + c * 8);
+          if (real) cp_async16(st + sw128_offset(row, c), src + kb * kBK + c * 8);
         cp_async_commit();
         if (pr == 0) {
           mbar_arrive_expect_tx(&full[s], b_bytes);
-          tma_load_3d(st + a_bytes, &mapGU, kb * kBK, 0, e * a.G, &full[s]);
+          tma_load_3d(smem + s * stage_bytes + 2 * a_bytes, &mapGU, kb * kBK, 0, e * a.G, &full[s]);
         }
         if (it >= LAG) {
-          if (LAG == 3) cp_async_wait<3>(); else cp_async_wait<2>();
+          if (LAG == 3) cp_async_wait<3>(); else if (LAG == 2) cp_async_wait<2>(); else cp_async_wait<1>();
           fence_proxy_async();
           mbar_arrive(&full[(it - LAG) % S]);
         }
@@ -350,62 +377,67 @@ gu_gemm_kernel(const __grid_constant__ CUtensorMap mapGU, const GUArgs a) {
     cp_async_wait<0>();
     fence_proxy_async();
     for (int j = max(0, it - LAG); j < it; ++j) mbar_arrive(&full[j % S]);
-  } else if (warp == 8 && lane == 0) {  // MMA issuer
+  } else if (warp == 16 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
-    int it = 0, tl = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
-      const int acc = tl & 1;
-      mbar_wait(&tempty[acc], ((tl >> 1) & 1) ^ 1, a.status);
+    int it = 0, ul = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
+      const bool two = pa.unit_tile[u] & 1;
+      mbar_wait_parked(tempty, (ul & 1) ^ 1, a.status);
       tc_fence_after();
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
-        mbar_wait(&full[s], (it / S) & 1, a.status);
+        mbar_wait_parked(&full[s], (it / S) & 1, a.status);
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + s * stage_bytes);
-        const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
+        const uint64_t ad0 = umma_desc_sw128(sa), ad1 = umma_desc_sw128(sa + a_bytes),
+                       bd = umma_desc_sw128(sa + 2 * a_bytes);
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k)
-          umma_bf16(tmem + acc * 256, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        for (int k = 0; k < kBK / 16; ++k) {
+          umma_bf16(tmem, ad0 + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          if (two) umma_bf16(tmem + 256, ad1 + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+        }
         umma_commit(&empty[s]);
       }
-      umma_commit(&tfull[acc]);
+      umma_commit(tfull);
     }
-  } else if (warp < 4) {  // epilogue: row r = pair; SwiGLU with the reference's rounding points
-    const int r = warp * 32 + lane;
-    int tl = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
-      const int acc = tl & 1;
-      mbar_wait(&tfull[acc], (tl >> 1) & 1, a.status);
+  } else if (warp < 8) {  // epilogue: row r of tile h = pair; SwiGLU with the reference's rounding points
+    const int h = warp >> 2, q = warp & 3, r = q * 32 + lane;
+    int ul = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
+      const int ut = pa.unit_tile[u];
+      mbar_wait_parked(tfull, ul & 1, a.status);
       tc_fence_after();
-      const int p = a.tile_row0[tile] + r;
-      const float wg = a.pair_w[p];
-      __nv_bfloat16* orow = a.a2 + (size_t)p * a.G;
-      for (int c0 = 0; c0 < NB; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
-        uint32_t pk[8];
+      if (h == 0 || (ut & 1)) {
+        const int p = a.tile_row0[(ut >> 1) + h] + r;
+        const float wg = a.pair_w[p];
+        __nv_bfloat16* orow = a.a2 + (size_t)p * a.G;
+        for (int c0 = 0; c0 < NB; c0 += 32) {
+          float v[32];
+          tmem_ld32(tmem + h * 256 + ((uint32_t)(q * 32) << 16) + c0, v);
+          uint32_t pk[8];
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          float o2[2];
+          for (int j = 0; j < 16; j += 2) {
+            float o2[2];
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const float gb = bf16r(v[2 * (j + q)]), ub = bf16r(v[2 * (j + q) + 1]);
-            const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
-            o2[q] = bf16r(bf16r(sb * ub) * wg);
+            for (int i = 0; i < 2; ++i) {
+              const float gb = bf16r(v[2 * (j + i)]), ub = bf16r(v[2 * (j + i) + 1]);
+              const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+              o2[i] = bf16r(bf16r(sb * ub) * wg);
+            }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(o2[0], o2[1]);
+            pk[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
           }
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(o2[0], o2[1]);
-          pk[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0 / 2);
+          dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + c0 / 2);
-        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
       tc_fence_before();
-      mbar_arrive(&tempty[acc]);
+      mbar_arrive(tempty);
     }
   }
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 16) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -426,7 +458,8 @@ constexpr int kDownStages = 2;
 
 __global__ void __launch_bounds__(192, 1)
 down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
-                 const __grid_constant__ CUtensorMap mapY, const DownArgs a) {
+                 const __grid_constant__ CUtensorMap mapYh, const __grid_constant__ CUtensorMap mapYl,
+                 const DownArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -463,12 +496,12 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     int tl = 0, ch = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
       const int e = a.tile_expert[tile], row0 = a.tile_row0[tile];
-      mbar_wait(aempty, (tl & 1) ^ 1, a.status);
+      mbar_wait_parked(aempty, (tl & 1) ^ 1, a.status);
       mbar_arrive_expect_tx(afull, a_bytes);
       for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + kb * a_kb, &mapA2, kb * kBK, row0, afull);
       for (int c = 0; c < NCH; ++c, ++ch) {
         const int s = ch % kDownStages;
-        mbar_wait(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
+        mbar_wait_parked(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
         mbar_arrive_expect_tx(&bfull[s], b_bytes);
         for (int kb = 0; kb < KB2; ++kb)
           tma_load_2d(sB + s * b_bytes + kb * b_kb, &mapD, kb * kBK, e * a.H + c * a.NCW, &bfull[s]);
@@ -478,12 +511,12 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
     int tl = 0, ch = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
-      mbar_wait(afull, tl & 1, a.status);
+      mbar_wait_parked(afull, tl & 1, a.status);
       tc_fence_after();
       for (int c = 0; c < NCH; ++c, ++ch) {
         const int s = ch % kDownStages, acc = ch & 1;
-        mbar_wait(&tempty[acc], ((ch >> 1) & 1) ^ 1, a.status);
-        mbar_wait(&bfull[s], (ch / kDownStages) & 1, a.status);
+        mbar_wait_parked(&tempty[acc], ((ch >> 1) & 1) ^ 1, a.status);
+        mbar_wait_parked(&bfull[s], (ch / kDownStages) & 1, a.status);
         tc_fence_after();
         for (int k16 = 0; k16 < a.G / 16; ++k16) {
           const int kb = k16 >> 2, kk = k16 & 3;
@@ -496,33 +529,56 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
       }
       umma_commit(aempty);
     }
-  } else if (warp < 4) {  // epilogue: the tile's fp32 rows, stored in pair order
-    // Per 32-column slice: every thread writes its row's 32 values into a 128-byte-swizzled
-    // [128 rows x 32] staging tile (conflict-free), the 4 epilogue warps meet at a named
-    // barrier, and one thread stores the whole 16 KB tile with a single TMA tensor store.
-    // Two staging tiles alternate; a tile is rewritten only after its store has read it.
+  } else if (warp < 4) {  // epilogue: the tile's rows, stored in pair order as 24-bit floats
+    // Each fp32 value is rounded to its top 24 bits (sign, exponent, 15 mantissa bits; relative
+    // error <= 2^-16) and split into a bf16 high plane and an 8-bit low plane, 3/4 of the
+    // fp32 bytes.  Per 64-column slice every thread writes its row into two swizzled staging
+    // tiles ([128 x 128 B] with the 128-byte swizzle, [128 x 64 B] with the 64-byte swizzle;
+    // both conflict-free), the 4 epilogue warps meet at a named barrier, and one thread stores
+    // both with TMA tensor stores (one bulk group).  Two staging pairs alternate; a pair is
+    // rewritten only after its stores have read it.
     const int r = warp * 32 + lane;
-    uint8_t* stg0 = stg;  // 2 x 16 KB, 1024-byte aligned
+    uint8_t* stg0 = stg;  // 2 x (16 KB + 8 KB), 1024-byte aligned
     int ch = 0, sub = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
       const int row0 = a.tile_row0[tile];
       for (int c = 0; c < NCH; ++c, ++ch) {
         const int acc = ch & 1;
-        mbar_wait(&tfull[acc], (ch >> 1) & 1, a.status);
+        mbar_wait_parked(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
-        for (int c0 = 0; c0 < a.NCW; c0 += 32, ++sub) {
-          uint8_t* buf = stg0 + (sub & 1) * 16384;
+        for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
+          uint8_t* hb = stg0 + (sub & 1) * 24576;
+          uint8_t* lb = hb + 16384;
           if (r == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);  // the buffer is free
-          float v[32];
-          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v);
+          named_bar_sync(1, 128);  // the buffers are free
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<float4*>(buf + sw128_offset(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int half = 0; half < 2; ++half) {
+            float v[32];
+            tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32 * half, v);
+            uint32_t u[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i]) + 0x80u;  // round at bit 8
+#pragma unroll
+            for (int j = 0; j < 4; ++j)  // high plane: 8 bf16 per 16-byte chunk
+              *reinterpret_cast<uint4*>(hb + sw128_offset(r, 4 * half + j)) =
+                  make_uint4(__byte_perm(u[8 * j], u[8 * j + 1], 0x7632), __byte_perm(u[8 * j + 2], u[8 * j + 3], 0x7632),
+                             __byte_perm(u[8 * j + 4], u[8 * j + 5], 0x7632), __byte_perm(u[8 * j + 6], u[8 * j + 7], 0x7632));
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {  // low plane: 16 bytes per chunk
+              uint32_t w4[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int b = 16 * j + 4 * q;
+                w4[q] = __byte_perm(__byte_perm(u[b], u[b + 1], 0x0051), __byte_perm(u[b + 2], u[b + 3], 0x0051), 0x5410);
+              }
+              *reinterpret_cast<uint4*>(lb + sw64_offset(r, 2 * half + j)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+          }
           fence_proxy_async();
-          named_bar_sync(1, 128);  // the tile is complete
+          named_bar_sync(1, 128);  // the tiles are complete
           if (r == 0) {
-            tma_store_2d(&mapY, buf, c * a.NCW + c0, row0);
+            tma_store_2d(&mapYh, hb, c * a.NCW + c0, row0);
+            tma_store_2d(&mapYl, lb, c * a.NCW + c0, row0);
             bulk_commit();
           }
         }
@@ -539,38 +595,70 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   }
 }
 
-// Per token: the fp32 rows of its pairs added in expert order (deterministic), rounded once
-// to bf16 (or written as fp32 partial sums for expert-parallel ranks).
+// Per token: the rows of its pairs (24-bit floats: bf16 high plane + 8-bit low plane) added
+// in expert order in fp32 (deterministic), rounded once to bf16 (or written as fp32 partial
+// sums for expert-parallel ranks).  Thread c owns columns 8c .. 8c + 7.
+__device__ __forceinline__ void unpack24(uint32_t h0, uint32_t h1, uint32_t l, float* f) {
+  f[0] = __uint_as_float((h0 << 16) | ((l & 0xFFu) << 8));
+  f[1] = __uint_as_float((h0 & 0xFFFF0000u) | (l & 0xFF00u));
+  f[2] = __uint_as_float((h1 << 16) | ((l >> 8) & 0xFF00u));
+  f[3] = __uint_as_float((h1 & 0xFFFF0000u) | ((l >> 16) & 0xFF00u));
+}
+
 template <bool F32OUT>
-__global__ void pair_combine_kernel(const float4* __restrict__ ypart, const int* __restrict__ tok_pairs,
-                                    const int* __restrict__ tok_k, int E, int H4, void* __restrict__ out) {
+__global__ void pair_combine_kernel(const uint4* __restrict__ yhi, const uint2* __restrict__ ylo,
+                                    const int* __restrict__ tok_pairs, const int* __restrict__ tok_k, int E, int H8,
+                                    void* __restrict__ out) {
   __shared__ int rows[256];
   const int t = blockIdx.x;
   const int k = tok_k[t];
   for (int j = threadIdx.x; j < k; j += blockDim.x) rows[j] = tok_pairs[(size_t)t * E + j];
   __syncthreads();
-  for (int c = threadIdx.x; c < H4; c += blockDim.x) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = threadIdx.x; c < H8; c += blockDim.x) {
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] = 0.f;
     int j = 0;
-    for (; j + 4 <= k; j += 4) {  // four independent loads in flight, added in order
-      float4 v[4];
+    for (; j + 4 <= k; j += 4) {  // four rows' loads in flight, added in order
+      uint4 h[4];
+      uint2 l[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) v[q] = ypart[(size_t)rows[j + q] * H4 + c];
+      for (int q = 0; q < 4; ++q) {
+        const size_t o = (size_t)rows[j + q] * H8 + c;
+        h[q] = yhi[o];
+        l[q] = ylo[o];
+      }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) { s.x += v[q].x; s.y += v[q].y; s.z += v[q].z; s.w += v[q].w; }
+      for (int q = 0; q < 4; ++q) {
+        float f[8];
+        unpack24(h[q].x, h[q].y, l[q].x, f);
+        unpack24(h[q].z, h[q].w, l[q].y, f + 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i] += f[i];
+      }
     }
     for (; j < k; ++j) {
-      const float4 v = ypart[(size_t)rows[j] * H4 + c];
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+      const size_t o = (size_t)rows[j] * H8 + c;
+      const uint4 h = yhi[o];
+      const uint2 l = ylo[o];
+      float f[8];
+      unpack24(h.x, h.y, l.x, f);
+      unpack24(h.z, h.w, l.y, f + 4);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s[i] += f[i];
     }
     if (F32OUT) {
-      static_cast<float4*>(out)[(size_t)t * H4 + c] = s;
+      float4* o = static_cast<float4*>(out) + ((size_t)t * H8 + c) * 2;
+      o[0] = make_float4(s[0], s[1], s[2], s[3]);
+      o[1] = make_float4(s[4], s[5], s[6], s[7]);
     } else {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      static_cast<uint2*>(out)[(size_t)t * H4 + c] = pk;
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(s[2 * i], s[2 * i + 1]);
+        pk[i] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      static_cast<uint4*>(out)[(size_t)t * H8 + c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   }
 }
@@ -612,20 +700,19 @@ static int make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t
   return PPMOE_OK;
 }
 
-// fp32 rank-2 map, 128-byte swizzle (32 floats per swizzle row), for tile stores.
-static int make_map_f32(CUtensorMap* m, const void* base, const cuuint64_t* dims, const cuuint64_t* strides_bytes,
-                        const cuuint32_t* box) {
+// Rank-2 map of any element type and swizzle, for the pair-row tile stores.
+static int make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, CUtensorMapSwizzle sw,
+                       const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is unavailable from the driver");
     return PPMOE_ERR_CUDA;
   }
   cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides_bytes, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides_bytes, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
-    set_error("cuTensorMapEncodeTiled (fp32) failed (%d)", (int)r);
+    set_error("cuTensorMapEncodeTiled (pair rows) failed (%d)", (int)r);
     return PPMOE_ERR_CUDA;
   }
   return PPMOE_OK;
@@ -714,7 +801,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sc_smem + 256 * 8 * 4)));
   count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, N, E, blockcnt);
   scan_kernel<<<1, 256, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
-                                 pair_token, pair_w, reinterpret_cast<long long*>(counts));
+                                 reinterpret_cast<int*>(ws + W.unit_tile), pair_token, pair_w, reinterpret_cast<long long*>(counts));
   scatter_kernel<<<W.nblocks, 256, sc_smem + 256 * 8 * 4, st>>>(weights, N, E, blockoff, exp_off, pair_token, pair_w,
                                                        reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
   PPMOE_CHECK_CUDA(cudaGetLastError());
@@ -722,32 +809,42 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   // ---- experts
   const int grid = (int)std::min<long long>(nsm, W.max_tiles);
   GUArgs ga{static_cast<const __nv_bfloat16*>(x), H, G, tile_expert, tile_row0, ntiles, pair_token, pair_w,
-            reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status, 2 * G <= 192 ? kGUMaxStages : 4};
-  const size_t g_smem = 1024 + (size_t)ga.stages * (kTileM * 128 + (size_t)2 * G * 128) + 256;
-  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g_smem));
-  gu_gemm_kernel<<<grid, 320, g_smem, st>>>(mGU, ga);
+            reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status, 0};
+  // stages of (2 A tiles + B) that fit in 227 KB of shared memory: 5 up to G = 32, 4 at
+  // G = 96, 3 at G = 128
+  const size_t pair_stage = 2 * kTileM * 128 + (size_t)2 * G * 128;
+  GUPairArgs pa{ga, reinterpret_cast<const int*>(ws + W.unit_tile)};
+  pa.g.stages = (int)std::min<size_t>(kGUMaxStages, (232448 - 1024 - 256) / pair_stage);
+  const size_t p_smem = 1024 + (size_t)pa.g.stages * pair_stage + 256;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p_smem));
+  gu_gemm_pair_kernel<<<grid, 544, p_smem, st>>>(mGU, pa);
   PPMOE_CHECK_CUDA(cudaGetLastError());
-  CUtensorMap mY;
+  CUtensorMap mYh, mYl;
+  uint8_t* y_hi = ws + W.ypart;
+  uint8_t* y_lo = y_hi + (size_t)W.max_pairs * H * 2;
   {
-    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)W.max_pairs}, st2[1] = {(cuuint64_t)H * 4};
-    cuuint32_t b[2] = {32, kTileM};
-    if ((rc = make_map_f32(&mY, ws + W.ypart, d, st2, b))) return rc;
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)W.max_pairs}, sh[1] = {(cuuint64_t)H * 2}, sl[1] = {(cuuint64_t)H};
+    cuuint32_t b[2] = {64, kTileM};
+    if ((rc = make_map_2d(&mYh, y_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_128B, d, sh, b))) return rc;
+    if ((rc = make_map_2d(&mYl, y_lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_64B, d, sl, b))) return rc;
   }
   DownArgs da{H, G, NCW, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
   const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
-                        2 * 16384 + 1024;
+                        2 * 24576 + 1024;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mY, da);
+  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, mYl, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   int* tok_pairs = reinterpret_cast<int*>(ws + W.tok_pairs);
   int* tok_k = reinterpret_cast<int*>(ws + W.tok_k);
-  const float4* yp = reinterpret_cast<const float4*>(ws + W.ypart);
+  const uint4* yh = reinterpret_cast<const uint4*>(y_hi);
+  const uint2* yl = reinterpret_cast<const uint2*>(y_lo);
+  const int H8 = H / 8, cthreads = std::min(256, (H8 + 31) / 32 * 32);
   if (mode == kPrefillExperts)
-    pair_combine_kernel<true><<<N, 128, 0, st>>>(yp, tok_pairs, tok_k, E, H / 4, out);
+    pair_combine_kernel<true><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);
   else
-    pair_combine_kernel<false><<<N, 128, 0, st>>>(yp, tok_pairs, tok_k, E, H / 4, out);
+    pair_combine_kernel<false><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
 }

@@ -39,6 +39,12 @@ __device__ __forceinline__ uint32_t sw128_offset(int r, int c) {
   return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
+// Byte offset of 16-byte chunk c (0..3) of row r inside a tile whose rows are 64 B, with the
+// 64-byte swizzle (chunk ^= (row / 2) % 4): the layout of CU_TENSOR_MAP_SWIZZLE_64B.
+__device__ __forceinline__ uint32_t sw64_offset(int r, int c) {
+  return (uint32_t)(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
 // ------------------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: start address >> 4 (bits 0-13),
 // leading byte offset 16 B (unused for swizzled K-major), stride byte offset 1024 B between
