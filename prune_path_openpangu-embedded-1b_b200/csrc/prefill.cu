@@ -343,25 +343,31 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8 && warp < 16) {  // producers: one gathered token row each; B via TMA
-    const int pr = tid - 256, h = pr >> 7, row = pr & 127;
-    const uint32_t aoff = h * a_bytes;
+  if (warp >= 8 && warp < 16) {  // producers: gathered token rows; B via TMA
+    // Producer warp pw fills rows (pw % 4) * 32 .. + 31 of tile pw / 4.  Per instruction its
+    // 32 lanes copy the 128-byte k-slices of 4 rows (8 lanes per row, one 16-byte chunk each),
+    // so every copy instruction reads 4 whole 128-byte lines.
+    const int pr = tid - 256, pw = warp - 8, h = pw >> 2, rbase = (pw & 3) * 32, sub = lane >> 3, ck = lane & 7;
+    uint8_t* const a_base = smem + h * a_bytes;
     int it = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
       const int ut = pa.unit_tile[u], t0 = ut >> 1;
       const int e = a.tile_expert[t0];
       // padding rows and the absent second tile load nothing: their stale shared-memory rows
       // only reach accumulator rows that the epilogue discards
-      const int tok = (h == 0 || (ut & 1)) ? a.pair_token[a.tile_row0[t0 + h] + row] : -1;
-      const bool real = tok >= 0;
-      const __nv_bfloat16* src = a.x + (size_t)(real ? tok : 0) * a.H;
+      const __nv_bfloat16* src[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int tok = (h == 0 || (ut & 1)) ? a.pair_token[a.tile_row0[t0 + h] + rbase + 4 * i + sub] : -1;
+        src[i] = tok >= 0 ? a.x + (size_t)tok * a.H + ck * 8 : nullptr;
+      }
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
         mbar_wait_parked(&empty[s], ((it / S) & 1) ^ 1, a.status);
-        uint8_t* st = smem + s * stage_bytes + aoff;
+        uint8_t* st = a_base + s * stage_bytes;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          if (real) cp_async16(st + sw128_offset(row, c), src + kb * kBK + c * 8);
+        for (int i = 0; i < 8; ++i)
+          if (src[i]) cp_async16(st + sw128_offset(rbase + 4 * i + sub, ck), src[i] + kb * kBK);
         cp_async_commit();
         if (pr == 0) {
           mbar_arrive_expect_tx(&full[s], b_bytes);
