@@ -305,8 +305,9 @@ constexpr int kGUMaxStages = 5;  // cp.async groups kept in flight per producer 
 // Gate/up over tile PAIRS: two 128-row tiles of one expert share every B (weight) stage, so
 // each expert's gate/up rows are read from L2 once per 256 pair rows instead of once per 128.
 // Per 64-wide k-block: two 128 x 2G x 16 MMAs per k step (accumulators at TMEM columns 0 and
-// 256).  Warps 0-7 are the epilogue (warp w: tile w / 4, TMEM lane quarter w % 4), warps
-// 8-15 gather the 256 token rows with cp.async, warp 16 allocates TMEM and issues the MMAs.
+// 256).  Warps 0-15 are the epilogue (warp w: tile w / 8, column half (w / 4) % 2, TMEM lane
+// quarter w % 4), warps 16-23 gather the 256 token rows with cp.async, warp 24 allocates TMEM
+// and issues the MMAs.
 // The one accumulator pair is not double-buffered (2 x 2G columns fill TMEM's 512), so a
 // unit's epilogue runs before the next unit's first MMA.
 struct GUPairArgs {
@@ -314,7 +315,7 @@ struct GUPairArgs {
   const int* unit_tile;  // per unit: first tile * 2 + (1 if the unit has a second tile)
 };
 
-__global__ void __launch_bounds__(544, 1)
+__global__ void __launch_bounds__(800, 1)
 gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs pa) {
   const GUArgs& a = pa.g;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -334,20 +335,20 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 257); mbar_init(&empty[s], 1); }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 256);
+    mbar_init(tempty, 512);
     fence_mbar_init();
   }
-  if (warp == 16) tmem_alloc(tmem_slot, 512);
+  if (warp == 24) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 8 && warp < 16) {  // producers: gathered token rows; B via TMA
+  if (warp >= 16 && warp < 24) {  // producers: gathered token rows; B via TMA
     // Producer warp pw fills rows (pw % 4) * 32 .. + 31 of tile pw / 4.  Per instruction its
     // 32 lanes copy the 128-byte k-slices of 4 rows (8 lanes per row, one 16-byte chunk each),
     // so every copy instruction reads 4 whole 128-byte lines.
-    const int pr = tid - 256, pw = warp - 8, h = pw >> 2, rbase = (pw & 3) * 32, sub = lane >> 3, ck = lane & 7;
+    const int pr = tid - 512, pw = warp - 16, h = pw >> 2, rbase = (pw & 3) * 32, sub = lane >> 3, ck = lane & 7;
     uint8_t* const a_base = smem + h * a_bytes;
     int it = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
@@ -383,7 +384,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     cp_async_wait<0>();
     fence_proxy_async();
     for (int j = max(0, it - LAG); j < it; ++j) mbar_arrive(&full[j % S]);
-  } else if (warp == 16 && lane == 0) {  // MMA issuer
+  } else if (warp == 24 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
     int it = 0, ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
@@ -406,8 +407,9 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
       }
       umma_commit(tfull);
     }
-  } else if (warp < 8) {  // epilogue: row r of tile h = pair; SwiGLU with the reference's rounding points
-    const int h = warp >> 2, q = warp & 3, r = q * 32 + lane;
+  } else if (warp < 16) {  // epilogue: row r of tile h = pair; SwiGLU with the reference's rounding points
+    const int h = warp >> 3, cw = (warp >> 2) & 1, q = warp & 3, r = q * 32 + lane;
+    const int cmid = NB / 64 * 32, cbeg = cw ? cmid : 0, cend = cw ? NB : cmid;  // this warp's columns
     int ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
       const int ut = pa.unit_tile[u];
@@ -417,7 +419,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
         const int p = a.tile_row0[(ut >> 1) + h] + r;
         const float wg = a.pair_w[p];
         __nv_bfloat16* orow = a.a2 + (size_t)p * a.G;
-        for (int c0 = 0; c0 < NB; c0 += 32) {
+        for (int c0 = cbeg; c0 < cend; c0 += 32) {
           float v[32];
           tmem_ld32(tmem + h * 256 + ((uint32_t)(q * 32) << 16) + c0, v);
           uint32_t pk[8];
@@ -443,7 +445,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     }
   }
   __syncthreads();
-  if (warp == 16) {
+  if (warp == 24) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -823,7 +825,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   pa.g.stages = (int)std::min<size_t>(kGUMaxStages, (232448 - 1024 - 256) / pair_stage);
   const size_t p_smem = 1024 + (size_t)pa.g.stages * pair_stage + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p_smem));
-  gu_gemm_pair_kernel<<<grid, 544, p_smem, st>>>(mGU, pa);
+  gu_gemm_pair_kernel<<<grid, 800, p_smem, st>>>(mGU, pa);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   CUtensorMap mYh, mYl;
   uint8_t* y_hi = ws + W.ypart;
