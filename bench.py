@@ -514,9 +514,9 @@ def main():
     for v in batched.values():
         v["hbm_frac"] = v["achieved_gbs"] / peaks()[0]
     batched["64"] = bench_batch64(P, dev, mods[:16], max(3, args.steps // 4), args.warmup)
-    pre = bench_prefill(P, dev, max(3, args.steps // 4), args.warmup) if world == 1 else None
+    pre = bench_prefill(P, dev, max(10, args.steps // 4), args.warmup) if world == 1 else None
     decr = bench_decoder(P, dev) if world == 1 and not args.no_decoder else None
-    epres = bench_ep(P, dev, world, rank, max(3, args.steps // 4), args.warmup, dist) if not args.no_ep else None
+    epres = bench_ep(P, dev, world, rank, max(10, args.steps // 4), args.warmup, dist) if not args.no_ep else None
     if rank == 0:
         cpu = cpu_baseline(base, xs_cpu[:8], args.cpu_seconds) if world == 1 else None
         line = {
