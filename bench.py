@@ -112,21 +112,38 @@ def decode_traffic(bytes_per_launch):
     return json.load(open(p))["traffic_over_algorithmic"] * bytes_per_launch
 
 
-def cpu_baseline(layers, xs, seconds=10.0):
-    """Oracle (reference algorithm, torch CPU bf16) decode bs1 on a bounded sample."""
+def decode_config(layers_per_step, world, pdl):
+    """The `config` of the decode line; identical for both arms (no measured quantities)."""
+    return {"workload": "decode bs1, one MoE-MLP layer (config 1)", "hidden": H, "experts": E, "group": G,
+            "tau": TAU, "router_scale": 3.5, "layers_per_step": layers_per_step, "pdl": bool(pdl),
+            "l2": "no flush: each step streams the distinct active weights of every layer (~12 MB per "
+                  "layer, far above the 126 MB L2 over a step)",
+            "parallelism": f"replicas x{world}"}
+
+
+def time_oracle_decode(layers, xs, seconds, min_calls=5, warm=2):
+    """Per-call wall times of the oracle (the reference algorithm's CPU path, torch CPU bf16,
+    all host threads) on single-token decode calls cycling over the given layers and inputs,
+    for about `seconds`.  Both CPU legs of this benchmark use it."""
     O = oracle()
     torch.set_num_threads(os.cpu_count() or 1)
-    for i in range(2):
+    for i in range(warm):
         O.moe_mlp(xs[i % len(xs)], layers[i % len(layers)], TAU)
     ts, n, t_end = [], 0, time.perf_counter() + seconds
-    while time.perf_counter() < t_end or n < 5:
+    while time.perf_counter() < t_end or n < min_calls:
         t0 = time.perf_counter()
         O.moe_mlp(xs[n % len(xs)], layers[n % len(layers)], TAU)
         ts.append(time.perf_counter() - t0)
         n += 1
+    return ts
+
+
+def cpu_baseline(layers, xs, seconds=10.0):
+    """Oracle (reference algorithm, torch CPU bf16) decode bs1 on a bounded sample."""
+    ts = time_oracle_decode(layers, xs, seconds)
     return {"value": statistics.median(ts) * 1e6, "unit": "us/layer", "cores": torch.get_num_threads(),
-            "kind": "port", "sample": f"{n} single-token calls over {len(layers)} layers "
-                                      f"(H={H}, E={E}, G={G}, tau={TAU}), median"}
+            "kind": "port", "sample": f"{len(ts)} single-token calls over {len(layers)} layers "
+                                      f"(H={H}, E={E}, G={G}, tau={TAU}), median per call"}
 
 
 def bench_prefill(P, dev, steps, warmup):
@@ -154,8 +171,8 @@ def bench_prefill(P, dev, steps, warmup):
     peak = peak_tflops()
     return {"workload": "prefill 8x2048 tokens, tau 0.70 (config 3)", "value": 16384 / us * 1e6,
             "unit": "tokens/s", "us_per_step": us, "steps": steps, "sum_k": k,
-            "roofline": {"bound": "tensor", "achieved": flops / us / 1e6, "peak": peak[0], "unit": "TFLOP/s",
-                         "frac": flops / us / 1e6 / peak[0], "peak_kind": peak[1]},
+            "roofline_bound": "tensor", "achieved_tflops": flops / us / 1e6, "peak_tflops": peak[0],
+            "roofline_frac": flops / us / 1e6 / peak[0], "peak_kind": peak[1], "flops_per_call": flops,
             "l2": "each step writes/reads ~1 GB of dispatch scratch (> L2)"}
 
 
@@ -237,8 +254,9 @@ def bench_decode_batch(P, dev, mods, n_tok, steps, warmup, stream):
     mods[0].check_device_status()
     us = e0.elapsed_time(e1) * 1e3 / (steps * len(mods))
     gbs = ubytes / len(mods) / (us * 1e-6) / 1e9
+    same = all(torch.equal(outs[l], m.forward_decode(xs[l])) for l, m in enumerate(mods))
     return {"tokens": n_tok, "us_per_layer": us, "tokens_per_s_per_layer": n_tok / (us * 1e-6),
-            "union_bytes_per_layer": ubytes / len(mods), "achieved_gbs": gbs}
+            "union_bytes_per_layer": ubytes / len(mods), "achieved_gbs": gbs, "graph_outputs_equal_eager": same}
 
 
 def bench_batch64(P, dev, mods, steps, warmup):
@@ -296,27 +314,30 @@ def run_reference(args, rank):
     if rank != 0:
         return
     synth = importlib.import_module(PKG).synth
-    O = oracle()
-    torch.set_num_threads(os.cpu_count() or 1)
-    nl = 4
-    layers = [synth.make_layer(s, H, E, G, router_scale=3.5) for s in range(nl)]
-    xs = [synth.make_tokens(s, 1, H) for s in range(nl)]
-    for w in range(args.warmup):
-        O.moe_mlp(xs[w % nl], layers[w % nl], TAU)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    # the same 4 weight sets and the same token rows as the GPU arm's first layers
+    layers = [synth.make_layer(s, H, E, G, router_scale=3.5) for s in range(4)]
+    xs = [synth.make_tokens(100 + l, 1, H) for l in range(8)]
+    # a step = one bounded sample of single-token layer calls (about cpu_seconds / steps of CPU
+    # time), per-call median like the GPU arm's cpu_baseline leg
+    per_step = max(0.5, args.cpu_seconds / max(args.steps, 1))
+    ts = time_oracle_decode(layers, xs, 0.0, min_calls=1, warm=max(args.warmup, 2))
     t0 = time.perf_counter()
-    for s in range(args.steps):
-        for l in range(nl):
-            O.moe_mlp(xs[(s + l) % nl], layers[l], TAU)
+    ts = []
+    for _ in range(args.steps):
+        ts += time_oracle_decode(layers, xs, per_step, min_calls=1, warm=0)
     dt = time.perf_counter() - t0
-    us = dt / (args.steps * nl) * 1e6
+    us = statistics.median(ts) * 1e6
+    cores = torch.get_num_threads()
     line = {"impl": "reference", "metric": METRIC, "value": us, "unit": "us/layer", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": "decode bs1, one MoE-MLP layer (config 1)", "hidden": H, "experts": E,
-                       "group": G, "tau": TAU, "layers_per_step": nl},
-            "cpu_baseline": {"value": us, "unit": "us/layer", "cores": torch.get_num_threads(), "kind": "port",
-                             "sample": f"{args.steps} steps x {nl} layers, dense-then-mask oracle"},
+            "data": "synthetic (seeded N(0,0.02) weights x4 distinct sets, N(0,1) activations)",
+            "config": decode_config(args.layers, world, not args.no_pdl),
+            "cpu_baseline": {"value": us, "unit": "us/layer", "cores": cores, "kind": "port",
+                             "sample": f"{len(ts)} single-token calls over 4 layers in {args.steps} steps, "
+                                       f"median per call (dense-then-mask oracle of MoEBlock / "
+                                       f"IntegratedOpenPanguMoEMLP, torch CPU bf16)"},
             "e2e": {"value": us, "unit": "us/layer", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -450,6 +471,10 @@ def main():
         dist.barrier()
     ms = e0.elapsed_time(e1)
     mods[0].check_device_status()
+    # outside the timed region: the graph's (PDL-chained) outputs equal plain eager calls bit for bit
+    ref_outs = [m.forward_decode(xs[l]) for l, m in enumerate(mods)]
+    torch.cuda.synchronize()
+    checks = {"pdl_graph_outputs_equal_eager": all(torch.equal(a, b) for a, b in zip(outs, ref_outs))}
     if dist:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -524,12 +549,10 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights x4 distinct sets, N(0,1) activations)",
-            "config": {"workload": "decode bs1, one MoE-MLP layer (config 1)", "hidden": H, "experts": E,
-                       "group": G, "tau": TAU, "router_scale": 3.5, "layers_per_step": args.layers,
-                       "mean_active_experts": sum(ks) / len(ks), "pdl": bool(pdl),
-                       "l2": "no flush: each step streams ~%.0f MB of distinct active weights (> 126 MB L2)"
-                             % (step_bytes / 1e6),
-                       "parallelism": f"replicas x{world}"},
+            "config": decode_config(args.layers, world, pdl),
+            "workload_stats": {"mean_active_experts": sum(ks) / len(ks), "step_bytes": step_bytes,
+                               "max_active_experts": max(ks), "min_active_experts": min(ks)},
+            "checks": checks,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": decode_traffic(step_bytes / args.layers), "bytes_per_launch": step_bytes / args.layers,

@@ -92,6 +92,24 @@ PPMOE_API int ppmoe_route_logits(const void* logits, int tokens, int experts, fl
 PPMOE_API int ppmoe_route_logits_train(const void* logits, int tokens, int experts, float tau,
                                        void* weights_out, uint8_t* mask_out, void* probs_out, void* stream);
 
+/* Router from token rows to a compact active-expert list per token: router GEMM (tcgen05) over
+ * the packed router rows, bf16 logits (+ optional fp32 prior logit_bias [E], then rounded to
+ * bf16), and the selection above.  Replaces moe_router_select_kernel_decode
+ * (src/tl_kernel_optimized_Ultimate_PanGU.py:335-380) and its outputs decode_active_idx,
+ * decode_active_weight, decode_num_active (tl:488-490, filled at tl:502-509), for any
+ * number of tokens:
+ *   active_ids [N][E] int32: token t's selected experts in descending softmax probability
+ *     (ties to the lower expert index), positions >= n_active[t] hold -1;
+ *   active_w [N][E] bf16: their gate weights sigmoid(logit) in the same order, 0 past the end;
+ *   n_active [N] int32: number of selected experts (>= 1: the forced top-1);
+ *   mask [N][E] uint8: optional dense selection mask (NULL to skip).
+ * Workspace: ppmoe_route_workspace_bytes(tokens, ...) bytes, 1024-byte aligned (no zeroing
+ * needed). */
+PPMOE_API size_t ppmoe_route_workspace_bytes(int tokens, int hidden, int experts, int group);
+PPMOE_API int ppmoe_route(const void* x, int tokens, const void* packed, int hidden, int experts, int group,
+                          float tau, const float* logit_bias, int32_t* active_ids, void* active_w,
+                          int32_t* n_active, uint8_t* mask, void* ws, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused decode, 1 <= tokens <= PPMOE_DECODE_MAX_TOKENS: router GEMV + selection + expert
  * SwiGLU + down projection in ONE launch.  Replaces TauSparseMoE.forward_decode
@@ -176,16 +194,26 @@ PPMOE_API int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts
  * that only hand over inputs and outputs, latency-critical paths where an allocation would
  * synchronise the device).  No counterpart in the reference.  Same kernel and results as
- * ppmoe_decode without bias and side outputs; its scratch is a ~1 MiB array inside this
+ * ppmoe_decode without bias and side outputs; its scratch is a ~2.9 MiB array inside this
  * library's device memory, held by every GPU that loads the library until process exit.
  *   Limit: 1 <= tokens <= 16 and tokens * hidden <= 8192 (PPMOE_ERR_UNSUPPORTED beyond).
  *   The first call on a device looks up the array's device address; make that first call
  *   before any stream capture.  All calls share the one array: calls that can overlap on
  *   the GPU (different streams, or different host threads) race and must be serialised by
- *   the caller.  Each call clears the array's status word and counters before its launch.
+ *   the caller.  Each call clears the array's status word and counters before its launch, so
+ *   read ppmoe_decode_noalloc_status after a call (before the next one) to learn whether the
+ *   device reported an error.
  * ------------------------------------------------------------------------------------- */
 PPMOE_API int ppmoe_decode_noalloc(const void* x, int tokens, const void* packed, int hidden, int experts,
                                    int group, float tau, void* out, void* stream);
+/* Device-side status of the ppmoe_decode_noalloc calls made so far on the current device:
+ * synchronises `stream` and returns PPMOE_OK, or PPMOE_ERR_TIMEOUT / PPMOE_ERR_WORKSPACE when a
+ * launch recorded a bounded wait that ran out or a capacity overflow (its output is then not
+ * valid); an error is cleared (status word and arrival counters re-armed) before returning.
+ * Like ppmoe_decode_noalloc it allocates nothing.  The cached scratch address belongs to the
+ * device's primary context: neither entry point may be used across cudaDeviceReset.
+ * No counterpart in the reference. */
+PPMOE_API int ppmoe_decode_noalloc_status(void* stream);
 
 /* Diagnostics: when `buf` (device, >= 32 * 8 bytes per CTA of the decode grid) is non-NULL,
  * later ppmoe_decode launches record per-CTA phase timestamps (SM clock64) into it; NULL

@@ -36,6 +36,9 @@ SIGNATURES = {
                                     _c_void_p]),
     "ppmoe_route_logits_train": (_c_int, [_c_void_p, _c_int, _c_int, _c_float, _c_void_p, _c_void_p,
                                           _c_void_p, _c_void_p]),
+    "ppmoe_route_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
+    "ppmoe_route": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
+                             _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_debug_trace": (None, [_c_void_p]),
     "ppmoe_prefill_workspace_bytes": (_c_size_t, [_c_int, _c_int, _c_int, _c_int]),
     "ppmoe_prefill_route": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
@@ -48,6 +51,7 @@ SIGNATURES = {
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_decode_noalloc": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
                                       _c_void_p, _c_void_p]),
+    "ppmoe_decode_noalloc_status": (_c_int, [_c_void_p]),
     "ppmoe_decode": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,
                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
                               _c_size_t, _c_int, _c_void_p]),

@@ -15,6 +15,8 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+void clear_error() { g_err[0] = 0; }
+
 int cuda_fail(cudaError_t e, const char* what) {
   set_error("%s failed: %s", what, cudaGetErrorString(e));
   return PPMOE_ERR_CUDA;
@@ -27,6 +29,10 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 void decode_set_trace(void*);
+size_t decode1_region_bytes(int H);
+size_t route_workspace_bytes(long long, int);
+int route_launch(const void*, int, const void*, int, int, int, float, const float*, int32_t*, void*, int32_t*,
+                 uint8_t*, void*, size_t, cudaStream_t);
 size_t prefill_workspace_bytes(long long, int, int, int);
 int prefill_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*, int64_t*,
                    void*, size_t, cudaStream_t, int);
@@ -90,7 +96,10 @@ int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_down, const v
 size_t ppmoe_workspace_bytes(int max_tokens, int hidden, int experts, int group) {
   if (check_shape("ppmoe_workspace_bytes", hidden, experts, group) || max_tokens < 0) return 0;
   const size_t nt = (size_t)(max_tokens < PPMOE_DECODE_MAX_TOKENS ? max_tokens : PPMOE_DECODE_MAX_TOKENS);
-  return kWsHeader + (size_t)kWsMaxClusters * (nt ? nt : 1) * hidden * 4;
+  // cross-cluster partials of the multi-token kernel, then the tagged partials of the
+  // single-token kernel
+  const size_t multi = (size_t)kWsMaxClusters * (nt ? nt : 1) * hidden * 4;
+  return kWsHeader + multi + decode1_region_bytes(hidden);
 }
 
 int ppmoe_workspace_init(void* ws, size_t ws_bytes, void* stream) {
@@ -116,8 +125,9 @@ int ppmoe_workspace_status(void* ws, void* stream) {
   PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
   if (word == 0) return PPMOE_OK;
   PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 4, st));
-  // a timed-out launch may have left arrival counters armed: re-arm them too
-  PPMOE_CHECK_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(ws) + kWsCounters, 0, 64, st));
+  // a timed-out launch may have left arrival counters armed: re-arm them too (words 0-7; word
+  // 8 is the single-token kernel's launch epoch, which must keep counting)
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(ws) + kWsCounters, 0, 32, st));
   PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
   if (word & DEVERR_TIMEOUT) {
     set_error("device: a bounded wait timed out (status 0x%x)", word);
@@ -321,6 +331,32 @@ int ppmoe_prefill_experts(const void* x, int tokens, const void* packed, int hid
   }
   return prefill_launch(x, tokens, packed, hidden, experts, group, 0.f, nullptr, out_f32, nullptr,
                         const_cast<void*>(weights), counts, ws, ws_bytes, static_cast<cudaStream_t>(stream), 2);
+}
+
+size_t ppmoe_route_workspace_bytes(int tokens, int hidden, int experts, int group) {
+  if (check_shape("ppmoe_route_workspace_bytes", hidden, experts, group) || tokens < 1) return 0;
+  return route_workspace_bytes(tokens, experts);
+}
+
+int ppmoe_route(const void* x, int tokens, const void* packed, int hidden, int experts, int group, float tau,
+                const float* logit_bias, int32_t* active_ids, void* active_w, int32_t* n_active, uint8_t* mask,
+                void* ws, size_t ws_bytes, void* stream) {
+  g_err[0] = 0;
+  if (int rc = check_shape("ppmoe_route", hidden, experts, group)) return rc;
+  if (tokens < 1) {
+    set_error("ppmoe_route: tokens=%d must be >= 1", tokens);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (!x || !packed || !active_ids || !active_w || !n_active || !ws) {
+    set_error("ppmoe_route: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (!aligned(x, 16) || !aligned(packed, 1024) || !aligned(ws, 1024)) {
+    set_error("ppmoe_route: x must be 16-byte, packed and ws 1024-byte aligned");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  return route_launch(x, tokens, packed, hidden, experts, group, tau, logit_bias, active_ids, active_w, n_active,
+                      mask, ws, ws_bytes, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

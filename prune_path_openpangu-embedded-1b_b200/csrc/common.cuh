@@ -16,6 +16,7 @@ namespace ppmoe {
 
 // ------------------------------------------------------------------ host error plumbing
 void set_error(const char* fmt, ...);
+void clear_error();  // empties the calling thread's last-error message
 int cuda_fail(cudaError_t e, const char* what);
 
 #define PPMOE_CHECK_CUDA(call)                                      \

@@ -14,11 +14,13 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 // Scratch limit: tokens * hidden <= 8192 (e.g. 5 tokens at hidden 1536, 4 at 2048, 16 at
-// 512) for up to 32 clusters of the decode grid: 32 * 8192 * 4 bytes of partials plus a
-// 256-byte header.  Every GPU that loads the library holds this ~1 MiB until exit.
+// 512) for up to 32 clusters of the multi-token decode grid (32 * 8192 * 4 bytes of
+// partials), plus the single-token kernel's tagged partials for hidden <= 1536 (160 CTAs x
+// 1536 x 8 bytes; at larger hidden sizes one token takes the multi-token kernel), plus a
+// 256-byte header.  Every GPU that loads the library holds these ~2.9 MiB until exit.
 constexpr int kNoAllocMaxTokHidden = 8192;
 constexpr size_t kNoAllocHeader = 256;
-constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4;
+constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4 + (size_t)160 * 1536 * 8;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -28,6 +30,9 @@ static std::mutex g_scratch_mu;
 
 // Device address of the scratch array on the current device (looked up once per device;
 // in host code the array's name is only a host-side stand-in, never a device address).
+// The cached address belongs to the device's current primary context: after
+// cudaDeviceReset the library's module is reloaded elsewhere and the address is stale, so
+// these entry points must not be used across a device reset.
 static int scratch_address(void** out) {
   int dev = 0;
   PPMOE_CHECK_CUDA(cudaGetDevice(&dev));
@@ -51,6 +56,7 @@ using namespace ppmoe;
 
 extern "C" int ppmoe_decode_noalloc(const void* x, int tokens, const void* packed, int hidden, int experts,
                                     int group, float tau, void* out, void* stream) {
+  clear_error();
   if (tokens < 1 || tokens > PPMOE_DECODE_MAX_TOKENS || hidden <= 0 ||
       (long long)tokens * hidden > kNoAllocMaxTokHidden) {
     set_error("ppmoe_decode_noalloc: tokens * hidden = %lld exceeds the built-in scratch limit %d "
@@ -75,11 +81,35 @@ extern "C" int ppmoe_decode_noalloc(const void* x, int tokens, const void* packe
   void* ws = nullptr;
   if (int rc = scratch_address(&ws)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // status word and arrival counters must start at zero (a previous call may have timed out)
-  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, kNoAllocHeader, st));
+  // status word and arrival counters must start at zero (a previous call may have timed out);
+  // the single-token kernel's epoch word (header word 24) keeps counting
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 96, st));
   uint8_t* w8 = static_cast<uint8_t*>(ws);
   return decode_launch(x, tokens, packed, hidden, experts, group, tau, nullptr, out, nullptr, nullptr, nullptr,
                        ws, kNoAllocBytes, 0, st, reinterpret_cast<uint32_t*>(w8),
                        reinterpret_cast<uint32_t*>(w8 + 64), reinterpret_cast<float*>(w8 + kNoAllocHeader),
                        kNoAllocBytes - kNoAllocHeader);
+}
+
+// Status of the allocation-free decode calls on the current device: synchronises `stream`,
+// reads the status word in the library-owned scratch (the bits a bounded device-side wait or
+// a capacity check set), and on an error re-arms the word and the arrival counters so that
+// the next call starts clean.  Mirrors ppmoe_workspace_status for the caller-workspace path.
+extern "C" int ppmoe_decode_noalloc_status(void* stream) {
+  clear_error();
+  void* ws = nullptr;
+  if (int rc = scratch_address(&ws)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t word = 0;
+  PPMOE_CHECK_CUDA(cudaMemcpyAsync(&word, ws, 4, cudaMemcpyDeviceToHost, st));
+  PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
+  if (word == 0) return PPMOE_OK;
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 96, st));
+  PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
+  if (word & DEVERR_TIMEOUT) {
+    set_error("ppmoe_decode_noalloc: a bounded device-side wait timed out (status 0x%x)", word);
+    return PPMOE_ERR_TIMEOUT;
+  }
+  set_error("ppmoe_decode_noalloc: capacity exceeded on the device (status 0x%x)", word);
+  return PPMOE_ERR_WORKSPACE;
 }

@@ -24,6 +24,7 @@ namespace ppmoe {
 
 int route_logits_launch(const void*, int, int, float, const float*, void*, uint8_t*, cudaStream_t,
                         void* probs_out = nullptr);
+int route_compact_launch(const void*, int, int, float, int32_t*, void*, int32_t*, uint8_t*, cudaStream_t);
 
 constexpr int kTileM = 128;
 constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
@@ -855,6 +856,45 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     pair_combine_kernel<false><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
+}
+
+// Router from token rows to the compact active-expert list: the tcgen05 router GEMM of the
+// prefill path (bf16 logits, optional prior) into the workspace, then route_compact_kernel.
+// Workspace: status word + N x E bf16 logits.
+size_t route_workspace_bytes(long long N, int E) { return 1024 + align_up((size_t)N * E * 2, 1024); }
+
+int route_launch(const void* x, int N, const void* packed, int H, int E, int G, float tau, const float* bias,
+                 int32_t* ids, void* w_out, int32_t* n_out, uint8_t* mask, void* wsp, size_t ws_bytes,
+                 cudaStream_t st) {
+  if (ws_bytes < route_workspace_bytes(N, E)) {
+    set_error("ppmoe_route: workspace %zu < %zu bytes needed for %d tokens", ws_bytes, route_workspace_bytes(N, E), N);
+    return PPMOE_ERR_WORKSPACE;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(wsp);
+  const PackedLayout PL = packed_layout(H, E, G);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws);
+  __nv_bfloat16* logits = reinterpret_cast<__nv_bfloat16*>(ws + 1024);
+  const int EP = (E + 15) / 16 * 16;
+  CUtensorMap mX, mR;
+  int rc;
+  {
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)N}, s[1] = {(cuuint64_t)H * 2};
+    cuuint32_t b[2] = {kBK, kTileM};
+    if ((rc = make_map(&mX, x, 2, d, s, b))) return rc;
+  }
+  {
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)E}, s[1] = {(cuuint64_t)H * 2};
+    cuuint32_t b[2] = {kBK, (cuuint32_t)EP};
+    if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
+  }
+  const int rstages = EP <= 128 ? 6 : 4;
+  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+  const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
+  router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return route_compact_launch(logits, N, E, tau, ids, w_out, n_out, mask, st);
 }
 
 }  // namespace ppmoe

@@ -57,6 +57,70 @@ __global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, in
   }
 }
 
+// Compact active-expert list per token, the form the reference's decode router hands to its
+// expert kernel (decode_active_idx / decode_active_weight / decode_num_active,
+// src/tl_kernel_optimized_Ultimate_PanGU.py:488-490, written by the kernel at tl:335-380):
+// ids[t][r] = the expert at position r of token t's selection in descending-probability
+// order (ties to the lower index), w[t][r] its gate weight, n[t] the count; positions
+// r >= n[t] hold id -1 and weight 0.  One warp per token; the kept experts are a prefix of
+// the sorted order, so each kept expert's position is the number of kept keys above its own.
+__global__ void route_compact_kernel(const __nv_bfloat16* __restrict__ logits, int N, int E, float tau_b,
+                                     int32_t* __restrict__ ids, __nv_bfloat16* __restrict__ w_out,
+                                     int32_t* __restrict__ n_out, uint8_t* __restrict__ mask_out) {
+  __shared__ __align__(16) uint32_t kbuf[8][256];
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const int t = blockIdx.x * (blockDim.x >> 5) + wi;
+  if (t >= N) return;
+  float l[kMaxExpertsPerLane], w[kMaxExpertsPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    l[i] = e < E ? __bfloat162float(logits[(size_t)t * E + e]) : -INFINITY;
+  }
+  uint32_t key[kMaxExpertsPerLane];
+  const uint32_t bits = select_experts_warp(l, E, tau_b, w, kbuf[wi], false, key);
+  __syncwarp();
+  // kept keys, compacted into the warp's buffer (any order)
+  int k = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const bool kept = (bits >> i) & 1u;
+    const uint32_t b = __ballot_sync(0xffffffffu, kept);
+    if (kept) kbuf[wi][k + __popc(b & ((1u << lane) - 1u))] = key[i];
+    k += __popc(b);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    const int e = lane + 32 * i;
+    if (e >= E) continue;
+    if ((bits >> i) & 1u) {
+      int r = 0;
+      #pragma unroll 4
+      for (int j = 0; j < k; ++j) r += kbuf[wi][j] > key[i];
+      ids[(size_t)t * E + r] = e;
+      w_out[(size_t)t * E + r] = __float2bfloat16_rn(w[i]);
+    }
+    if (e >= k) {
+      ids[(size_t)t * E + e] = -1;
+      w_out[(size_t)t * E + e] = __float2bfloat16_rn(0.f);
+    }
+    if (mask_out) mask_out[(size_t)t * E + e] = (bits >> i) & 1u;
+  }
+  if (lane == 0) n_out[t] = k;
+}
+
+int route_compact_launch(const void* logits, int N, int E, float tau, int32_t* ids, void* w_out, int32_t* n_out,
+                         uint8_t* mask_out, cudaStream_t st) {
+  if (N == 0) return PPMOE_OK;
+  const int warps = 8;
+  route_compact_kernel<<<(N + warps - 1) / warps, warps * 32, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(logits), N, E, __bfloat162float(__float2bfloat16_rn(tau)), ids,
+      static_cast<__nv_bfloat16*>(w_out), n_out, mask_out);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return PPMOE_OK;
+}
+
 int route_logits_launch(const void* logits, int N, int E, float tau, const float* bias, void* w_out,
                         uint8_t* mask_out, cudaStream_t st, void* probs_out = nullptr);
 int route_logits_launch(const void* logits, int N, int E, float tau, const float* bias, void* w_out,

@@ -220,7 +220,8 @@ __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPer
 // by p descending and then by expert index ascending.
 __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
                                                         float tau_b, float (&w)[kMaxExpertsPerLane],
-                                                        uint32_t* kbuf, bool throughput = false) {
+                                                        uint32_t* kbuf, bool throughput = false,
+                                                        uint32_t* keys_out = nullptr) {
   const int lane = threadIdx.x & 31;
   uint32_t mk = 0u;
 #pragma unroll
@@ -255,6 +256,10 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   else if (E <= 64) done = throughput ? select_parallel<2>(key, E, tau_b, bits) : select_rank<2>(key, E, tau_b, bits, kbuf);
   else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
   else done = select_parallel<8>(key, E, tau_b, bits);
+  if (keys_out) {
+#pragma unroll
+    for (int i = 0; i < kMaxExpertsPerLane; ++i) keys_out[i] = key[i];
+  }
   if (!done) bits = select_sequential(key, E, tau_b);
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i)

@@ -27,7 +27,8 @@ __all__ = ["TauSparseMoE", "IntegratedOpenPanguMoEMLP", "physical_reorder_for_in
 
 
 def _stream_handle(device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """Raw handle of the current CUDA stream of ``device`` (no Stream object is built)."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None else torch.cuda.current_device())
 
 
 class TauSparseMoE(nn.Module):
@@ -58,11 +59,23 @@ class TauSparseMoE(nn.Module):
         self._ws_tokens = 0
         self._pws = None
         self._pws_tokens = 0
+        # persistent decode output (the reference's decode_out, tl:491, returned as a view at
+        # tl:530): forward() of <= 16 tokens returns a view of it that the next decode call
+        # of this module overwrites
+        self._dec_out = None
+        self._dec_views = {}
+        self._bias_src = None
+        self._bias_ver = -1
+        self._bias_dev = None
 
     # ------------------------------------------------------------------ packing
     def _weights_key(self):
-        return tuple((t.data_ptr(), t._version, t.device) for t in
-                     (self.W_gate, self.W_up, self.W_down, self.router))
+        # identity of the four buffers' storage and their in-place version counters (a
+        # reassignment of .data changes the pointer, an in-place edit bumps _version)
+        b = self._buffers
+        g, u, d, r = b["W_gate"], b["W_up"], b["W_down"], b["router"]
+        return (g.data_ptr(), g._version, u.data_ptr(), u._version, d.data_ptr(), d._version,
+                r.data_ptr(), r._version)
 
     def packed(self) -> torch.Tensor:
         """The packed weight blob (uint8, 1 KiB aligned), rebuilt if any buffer changed."""
@@ -111,9 +124,7 @@ class TauSparseMoE(nn.Module):
         N, H = x_flat.shape
         out = torch.empty(N, H, dtype=torch.bfloat16, device=x_flat.device)
         ws = self.workspace(N)
-        bias = self.logit_bias
-        if bias is not None:
-            bias = bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
+        bias = self._device_bias(x_flat.device)
         counts = self.activated_statistics if self.track_statistics else None
         _lib.call("ppmoe_decode", x_flat.data_ptr(), N, self.packed().data_ptr(), H,
                   self.num_experts, self.group_size, float(self.tau), _lib.ptr(bias),
@@ -140,9 +151,7 @@ class TauSparseMoE(nn.Module):
         N, H = x_flat.shape
         out = torch.empty(N, H, dtype=torch.bfloat16, device=x_flat.device)
         ws = self.prefill_workspace(N)
-        bias = self.logit_bias
-        if bias is not None:
-            bias = bias.to(device=x_flat.device, dtype=torch.float32).contiguous()
+        bias = self._device_bias(x_flat.device)
         counts = self.activated_statistics if self.track_statistics else None
         _lib.call("ppmoe_prefill", x_flat.data_ptr(), N, self.packed().data_ptr(), H, self.num_experts,
                   self.group_size, float(self.tau), _lib.ptr(bias), out.data_ptr(), _lib.ptr(logits_out),
@@ -150,14 +159,84 @@ class TauSparseMoE(nn.Module):
                   _stream_handle(x_flat.device))
         return out
 
+    def route(self, x_flat: torch.Tensor, *, mask_out=None):
+        """Compact active-expert lists for ``x_flat [N,H]`` (``ppmoe_route``): returns
+        ``(ids [N,E] int32, weights [N,E] bf16, n_active [N] int32)``, each row's selected
+        experts in descending probability with -1 / 0 past ``n_active`` -- the decode router
+        outputs of the reference (tl:488-490, tl:502-509) for any token count."""
+        N, H = x_flat.shape
+        dev = x_flat.device
+        E = self.num_experts
+        ids = torch.empty(N, E, dtype=torch.int32, device=dev)
+        w = torch.empty(N, E, dtype=torch.bfloat16, device=dev)
+        n = torch.empty(N, dtype=torch.int32, device=dev)
+        nbytes = _lib.load().ppmoe_route_workspace_bytes(N, H, E, self.group_size)
+        buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=dev)
+        ws = buf[(-buf.data_ptr()) % 1024:][:nbytes]
+        bias = self.logit_bias
+        if bias is not None:
+            bias = bias.to(device=dev, dtype=torch.float32).contiguous()
+        x_flat = x_flat.to(torch.bfloat16).contiguous()
+        _lib.call("ppmoe_route", x_flat.data_ptr(), N, self.packed().data_ptr(), H, E, self.group_size,
+                  float(self.tau), _lib.ptr(bias), ids.data_ptr(), w.data_ptr(), n.data_ptr(),
+                  _lib.ptr(mask_out), ws.data_ptr(), nbytes, _stream_handle(dev))
+        return ids, w, n
+
+    def _device_bias(self, dev):
+        b = self.logit_bias
+        if b is None:
+            return None
+        if b is not self._bias_src or b._version != self._bias_ver or self._bias_dev.device != dev:
+            self._bias_src, self._bias_ver = b, b._version
+            self._bias_dev = b.to(device=dev, dtype=torch.float32).contiguous()
+        return self._bias_dev
+
+    def _decode_into_persistent(self, x, B, L, H):
+        """forward() for <= 16 tokens: one ctypes call into ppmoe_decode writing the persistent
+        output buffer; the view returned aliases it (as the reference's decode_out does)."""
+        dev = x.device
+        key = self._weights_key()
+        if self._packed is None or self._packed_key != key:
+            self.packed()
+        out = self._dec_out
+        if out is None or out.device != dev:
+            out = self._dec_out = torch.empty(_lib.DECODE_MAX_TOKENS, H, dtype=torch.bfloat16, device=dev)
+            self._dec_views = {}
+        ws = self._ws
+        if ws is None or self._ws_tokens < _lib.DECODE_MAX_TOKENS or ws.device != dev:
+            ws = self.workspace(_lib.DECODE_MAX_TOKENS)
+        view = self._dec_views.get((B, L))
+        if view is None:
+            view = self._dec_views[(B, L)] = out[:B * L].view(B, L, H)
+        bias = self._device_bias(dev)
+        counts = self._buffers["activated_statistics"] if self.track_statistics else None
+        rc = _lib.load().ppmoe_decode(x.data_ptr(), B * L, self._packed.data_ptr(), H, self.num_experts,
+                                      self.group_size, float(self.tau),
+                                      None if bias is None else bias.data_ptr(), out.data_ptr(), None, None,
+                                      None if counts is None else counts.data_ptr(), ws.data_ptr(), ws.numel(), 0,
+                                      _stream_handle(dev))
+        if rc:
+            raise _lib.PPMoEError("ppmoe_decode", rc, _lib.load().ppmoe_last_error().decode())
+        return view
+
     def forward(self, x: torch.Tensor, **kw) -> torch.Tensor:
+        """``[B,L,H] -> [B,L,H]`` bf16 (tl:606-615).  Up to 16 tokens: the fused decode
+        kernel, returning a view of a persistent per-module output buffer (overwritten by the
+        module's next decode call, like the reference's decode_out); more tokens: prefill into
+        a fresh tensor."""
         B, L, H = x.shape
         N = B * L
         if x.device.type != "cuda":
             raise RuntimeError("TauSparseMoE runs on CUDA only; got a tensor on " + str(x.device))
-        x_flat = x.reshape(N, H).to(torch.bfloat16).contiguous()
+        if x.dtype is not torch.bfloat16:
+            x = x.to(torch.bfloat16)
+        if not x.is_contiguous():
+            x = x.contiguous()
         if N == 0:
             return torch.empty(B, L, H, dtype=torch.bfloat16, device=x.device)
+        if N <= _lib.DECODE_MAX_TOKENS and not kw:
+            return self._decode_into_persistent(x, B, L, H)
+        x_flat = x.view(N, H)
         if N <= _lib.DECODE_MAX_TOKENS:
             return self.forward_decode(x_flat, **kw).view(B, L, H)
         return self.forward_prefill(x_flat, **kw).view(B, L, H)

@@ -22,6 +22,28 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device")
 
 
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """End-to-end mask parity against the literal reference (unstable CPU sort), summed over
+    every GPU parity check of the session: tokens, mismatching tokens and their causes."""
+    try:
+        from gpu_helpers import L2_STATS
+    except ImportError:
+        return
+    if not L2_STATS:
+        return
+    n = sum(s[1] for s in L2_STATS)
+    m = sum(s[2] for s in L2_STATS)
+    causes = {}
+    for s in L2_STATS:
+        for k, v in s[3].items():
+            causes[k] = causes.get(k, 0) + v
+    terminalreporter.write_line(f"mask parity vs literal reference: {m} of {n} tokens differ "
+                                f"({100.0 * m / max(n, 1):.3f}%), all explained: {causes}")
+    for what, nt, mm, c in L2_STATS:
+        if mm:
+            terminalreporter.write_line(f"  {what}: {mm}/{nt} {c}")
+
+
 def pkg():
     return importlib.import_module(PKG_NAME)
 

@@ -79,6 +79,50 @@ def assert_selection_matches(w, lg, tau, what=""):
     return int(bad.sum())
 
 
+# Per-test end-to-end mask agreement with the literal reference (collected for the summary
+# printed at the end of the session by conftest.py)
+L2_STATS = []
+
+
+def assert_mask_l2(x, L, tau, lg, w, bias=None, what="", ref_logits=None):
+    """End-to-end selection parity with the LITERAL reference path (unstable CPU sort on the
+    oracle's own router logits, src/MoEBlock.py:68-86).  Every token whose mask differs must
+    be explained by one of:
+      * "logit": the GPU's router logits of that token differ from the oracle's (<= 1 bf16 ulp,
+        fp32 summation order) and the GPU mask equals the oracle's selection on the GPU's
+        logits;
+      * "tie": the oracle's stable and unstable selections differ on its own logits (equal
+        bf16 probabilities straddle the cutoff) and the GPU mask equals the stable one;
+      * "rounding": a probability or sigmoid of the token sits on a bf16 rounding midpoint to
+        fp32 precision (CPU and GPU exp implementations differ there).
+    Returns (tokens, mismatches, counts by cause) and records them in L2_STATS."""
+    O = oracle()
+    ref_lg = O.router_logits(x, L.router_w, bias) if ref_logits is None else ref_logits
+    _, lit = O.softmax_thresholding(ref_lg, tau, stable=False)
+    _, st = O.softmax_thresholding(ref_lg, tau, stable=True)
+    _, st_gpu = O.softmax_thresholding(lg, tau, stable=True)
+    gm = (w > 0).reshape(lit.shape)
+    diff = (gm != lit).any(-1).flatten()
+    n = int(diff.numel())
+    causes = {"logit": 0, "tie": 0, "rounding": 0}
+    if bool(diff.any()):
+        lg2, rl2 = lg.reshape(n, -1), ref_lg.reshape(n, -1)
+        gm2, st2, stg2, lit2 = gm.reshape(n, -1), st.reshape(n, -1), st_gpu.reshape(n, -1), lit.reshape(n, -1)
+        for t in diff.nonzero().flatten().tolist():
+            if not torch.equal(lg2[t], rl2[t]) and torch.equal(gm2[t], stg2[t]):
+                causes["logit"] += 1
+            elif not torch.equal(st2[t], lit2[t]) and torch.equal(gm2[t], st2[t]):
+                causes["tie"] += 1
+            elif bool(ambiguous_tokens(lg2[t:t + 1]).all()):
+                causes["rounding"] += 1
+            else:
+                raise AssertionError(f"{what}: token {t} selects {gm2[t].nonzero().flatten().tolist()}, the "
+                                     f"reference {lit2[t].nonzero().flatten().tolist()}: unexplained")
+    mism = int(diff.sum())
+    L2_STATS.append((what, n, mism, dict(causes)))
+    return n, mism, causes
+
+
 def check_against_oracle(L, x, tau, out, lg, w, bias=None, what=""):
     """Router logits within 1 bf16 ulp of the oracle's; selection bit-exact given the GPU's
     logits (stable contract); output within tolerance of the oracle teacher-forced with the
@@ -95,7 +139,10 @@ def check_against_oracle(L, x, tau, out, lg, w, bias=None, what=""):
     assert_selection_matches(w, lg, tau, what)
     tf = O.moe_mlp(x, L, tau, logits=lg)
     assert_close_out(out, tf.out, what)
-    sel_diff = int(((w > 0) != (ref.weights > 0)).any(-1).sum())
-    if sel_diff == 0:
-        assert_close_out(out, ref.out, what + " (end to end)")
+    assert_mask_l2(x, L, tau, lg, w, bias=bias, what=what, ref_logits=ref.logits)
+    # end to end against the oracle's own output on the tokens whose selection agrees
+    agree = ~((w > 0) != (ref.weights > 0)).any(-1)
+    if bool(agree.any()):
+        assert_close_out(out[agree], ref.out[agree], what + " (end to end)")
+    sel_diff = int((~agree).sum())
     return int((nd > 0).sum()), sel_diff

@@ -5,7 +5,8 @@ import torch
 import torch.nn.functional as F
 
 from conftest import MAX_ABS, MEAN_REL, assert_close_out, oracle, pkg
-from gpu_helpers import assert_selection_matches, check_against_oracle, make_layer, make_module, run_decode
+from gpu_helpers import (assert_mask_l2, assert_selection_matches, check_against_oracle, make_layer,
+                         make_module, run_decode)
 
 pytestmark = pytest.mark.gpu
 
@@ -47,10 +48,13 @@ def test_decode_golden_cases(golden, cuda):
         x = synth.make_tokens(c["seed"], c["tokens"], c["hidden"])
         m = make_module(L, c["tau"], cuda)
         out, lg, w = run_decode(m, x, cuda)
-        n_ulp, n_sel = check_against_oracle(L, x, c["tau"], out, lg, w, what=c["name"])
-        # against the reference's literal (unstable-sort) golden output
-        if torch.equal(w > 0, c["weights"] > 0):
-            assert_close_out(out, c["out"], c["name"] + " vs reference golden")
+        check_against_oracle(L, x, c["tau"], out, lg, w, what=c["name"])
+        # against the reference's own recorded selection (literal unstable sort on its own
+        # logits): every differing token explained, the others' outputs within tolerance
+        assert_mask_l2(x, L, c["tau"], lg, w, what=c["name"] + " vs reference golden", ref_logits=c["logits"])
+        agree = ~((w > 0) != (c["weights"] > 0)).any(-1)
+        if bool(agree.any()):
+            assert_close_out(out[agree], c["out"][agree], c["name"] + " vs reference golden")
 
 
 @pytest.mark.parametrize("tau", [0.70, 0.95])

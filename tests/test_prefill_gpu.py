@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from conftest import assert_close_out, oracle, pkg
-from gpu_helpers import assert_selection_matches, make_layer, make_module, ulp_diff_bf16
+from gpu_helpers import assert_mask_l2, assert_selection_matches, make_layer, make_module, ulp_diff_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -26,6 +26,7 @@ def check(L, x, tau, out, lg, w, bias=None, what=""):
     assert_selection_matches(w, lg, tau, what)
     tf = O.moe_mlp(x, L, tau, logits=lg)
     assert_close_out(out, tf.out, what)
+    assert_mask_l2(x, L, tau, lg, w, bias=bias, what=what, ref_logits=ref_lg)
 
 
 @pytest.mark.parametrize("shape", [(256, 16, 32, 300, 0.7), (1536, 64, 96, 64, 0.95), (1536, 64, 96, 17, 0.7),
@@ -77,3 +78,19 @@ def test_prefill_zipf_bias(cuda):
     check(L, x, tau, out, lg, w, bias=b, what="zipf")
     out2, lg2, w2 = run_prefill(m, x, cuda, bias=b.to(cuda))  # fixed-order sums: bit-reproducible
     assert torch.equal(out2, out) and torch.equal(w2, w) and torch.equal(lg2, lg)
+
+
+@pytest.mark.parametrize("tau", [0.70, 0.95])
+def test_batch64_sweep(cuda, tau):
+    """Config 2 at 64 tokens (the module sends more than 16 tokens to the prefill path):
+    seeds 0-3 at both taus, full layer shape, against the oracle (logits, selection, output,
+    end-to-end masks against the literal reference)."""
+    H, E, G = 1536, 64, 96
+    for seed in range(4):
+        L = make_layer(seed, H, E, G, tau)
+        x = pkg().synth.make_tokens(seed, 64, H, stream=1)
+        m = make_module(L, tau, cuda)
+        out, lg, w = run_prefill(m, x, cuda)
+        check(L, x, tau, out, lg, w, what=f"b64 tau{tau} s{seed}")
+        y = m(x.view(1, 64, H).to(cuda)).view(64, H).cpu()  # the module takes the same path
+        assert torch.equal(y, out)

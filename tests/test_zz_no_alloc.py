@@ -30,7 +30,10 @@ def test_decode_noalloc_matches_workspace_decode(cuda, tokens):
         out = torch.empty(tokens, H, dtype=torch.bfloat16, device=cuda)
         lib.call("ppmoe_decode_noalloc", x.data_ptr(), tokens, packed.data_ptr(), H, E, G, tau,
                  out.data_ptr(), stream)
-        torch.cuda.synchronize()
+        # the device status word lives in the library's own scratch: read it back (and
+        # check that no bounded wait ran out) before the next call clears it
+        lib.call("ppmoe_decode_noalloc_status", stream)
+        assert lib.load().ppmoe_last_error() == b""
         assert_close_out(out.cpu(), ref.cpu(), f"noalloc call {call}")
         assert torch.equal(out.cpu(), ref.cpu())  # same kernel, same order of operations
 
