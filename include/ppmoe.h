@@ -164,7 +164,10 @@ PPMOE_API int ppmoe_prefill(const void* x, int tokens, const void* packed, int h
 /* Router half of ppmoe_prefill (router GEMM + selection): gate weights [N][E] bf16 (0 where
  * unselected) into weights_out, bf16 logits into logits_out (optional).  Replaces
  * moe_router_kernel + torch.sort + moe_select_expert_kernel + scatter_ (tl:40-124, 550-564).
- * Used by expert-parallel prefill on each rank's token shard. */
+ * Used by expert-parallel prefill on each rank's token shard.  Needs only
+ * ppmoe_route_workspace_bytes(tokens, ...) bytes of workspace, and reads only the router
+ * section of `packed` (its first E * H * 2 bytes: router_eh [E][H]), so a 1024-byte aligned
+ * buffer holding just those rows serves as `packed`. */
 PPMOE_API int ppmoe_prefill_route(const void* x, int tokens, const void* packed, int hidden, int experts,
                                   int group, float tau, const float* logit_bias, void* logits_out,
                                   void* weights_out, void* ws, size_t ws_bytes, void* stream);
@@ -194,7 +197,7 @@ PPMOE_API int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts
  * that only hand over inputs and outputs, latency-critical paths where an allocation would
  * synchronise the device).  No counterpart in the reference.  Same kernel and results as
- * ppmoe_decode without bias and side outputs; its scratch is a ~2.9 MiB array inside this
+ * ppmoe_decode without bias and side outputs; its scratch is a ~1.2 MiB array inside this
  * library's device memory, held by every GPU that loads the library until process exit.
  *   Limit: 1 <= tokens <= 16 and tokens * hidden <= 8192 (PPMOE_ERR_UNSUPPORTED beyond).
  *   The first call on a device looks up the array's device address; make that first call

@@ -63,9 +63,9 @@ struct DecodeArgs {
   unsigned long long* trace;  // optional per-CTA phase timestamps [grid][32] (diagnostics)
 };
 
-__device__ __forceinline__ unsigned long long clk64() {
+__device__ __forceinline__ unsigned long long clk64() {  // diagnostics stamp: global ns timer
   unsigned long long c;
-  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(c));
   return c;
 }
 #define PPMOE_TRACE(i) \
@@ -950,19 +950,20 @@ void decode_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(bu
 
 int decode1_launch(const void* x, const void* packed, int H, int E, int G, float tau, const float* bias, void* out,
                    void* logits_out, void* weights_out, int64_t* counts, int pdl, cudaStream_t stream,
-                   uint32_t* status, uint32_t* epoch, void* part, size_t part_bytes, unsigned long long* trace);
-size_t decode1_region_bytes(int H);
+                   uint32_t* status, uint32_t* epoch, void* region, size_t region_bytes,
+                   unsigned long long* trace);
+size_t decode1_region_bytes(int E, int G);
 
 int decode_launch(const void* x, int tokens, const void* packed, int H, int E, int G, float tau,
                   const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
                   void* wsp, size_t ws_bytes, int pdl, cudaStream_t stream, uint32_t* status,
                   uint32_t* counters, float* cpart, size_t cpart_bytes, int x_host) {
-  // The single-token kernel (decode1.cu) where its shape limits allow.  Its tagged partials
-  // live at the END of the partial area (this kernel's cluster partials at its start), so the
+  // The single-token kernel (decode1.cu) where its shape limits allow.  Its exchange region
+  // lives at the END of the partial area (this kernel's cluster partials at its start), so the
   // two never overlap in a workspace sized by ppmoe_workspace_bytes; its epoch word is word 8
   // of the counter line (this kernel uses words 0-7).
   if (tokens == 1) {
-    const size_t r1 = decode1_region_bytes(H);
+    const size_t r1 = decode1_region_bytes(E, G);
     if (cpart_bytes >= r1) {
       const size_t off = (cpart_bytes - r1) & ~(size_t)255;
       const int rc = decode1_launch(x, packed, H, E, G, tau, bias, out, logits_out, weights_out, counts, pdl, stream,

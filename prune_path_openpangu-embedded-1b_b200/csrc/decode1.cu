@@ -13,28 +13,32 @@
 //
 //  1. Router.  Rank r of a pair holds the router rows of experts [r E/2, (r+1) E/2) (bulk
 //     copies issued before the dependency wait) and computes their logits on the tensor cores
-//     (mma.sync m16n8k16, the token as A row 0, 8 experts' router rows as the B columns, warps
-//     split K, partial sums added in warp order); each logit goes to the peer with st.async
-//     (completing on the peer's mbarrier).  Every pair computes bit-identical logits.
+//     (mma.sync m16n8k16, the token as A row 0, 8 experts' router rows as the B columns, one
+//     accumulator chain per expert tile and k parity, warps split K, partial sums added in
+//     warp order); each logit goes to the peer with st.async (completing on the peer's
+//     mbarrier).  Every pair computes bit-identical logits.
 //  2. Selection (select.cuh, CTA-wide rank count), redundantly per CTA.
-//  3. Experts.  The union's |U| G neurons are split evenly over the grid; each neuron's record
-//     (gate row | up row | down row, contiguous in the packed blob) is one bulk copy into a
-//     shared-memory slot.  Gate/up on the tensor cores (the token as A row 0, 4 neurons'
-//     gate/up rows as the 8 B columns; the k order inside each 16-wide step is permuted
-//     identically for A and B so that every fragment is one 8-byte load), SwiGLU and the gate
-//     weight per neuron, down rows by hidden column in fp32.  More neurons than slots: rounds.
-//  4. Reduction.  Every CTA stores its fp32 partial [H] as 64-bit words (value | launch epoch
-//     << 32); CTA c polls the words of its 1/grid slice of the hidden columns in every
-//     partial until all carry this launch's epoch (no flag, fence or atomic on the critical
-//     path), sums them in a fixed order and writes bf16.  CTA 0 advances the epoch word after
-//     its own sums, i.e. after every CTA has read the epoch.  Deterministic; one bf16
-//     rounding.  The polls need every CTA of the grid resident: the grid is one CTA per SM
-//     (two fit), and with programmatic dependent launch a grid is only launched after every
-//     CTA of its predecessor is running.
+//  3. Gate/up by neuron.  The union's |U| G neurons are split evenly over the grid; each
+//     neuron's gate and up rows (the first 4H bytes of its packed record) are one bulk copy
+//     into a shared-memory slot; warp w computes the dot products of its neurons with the
+//     token (fp32 FMA, lanes split K, butterfly sum), SwiGLU and the gate weight, and
+//     publishes a2 = bf16(bf16(silu(g) u) w) as a 64-bit word (value | launch epoch << 32).
+//  4. Down projection by hidden column.  CTA c owns columns [c H / grid, (c+1) H / grid); the
+//     K-major down rows of those columns for every selected expert (down_t [E][H][G] of the
+//     packed blob, one bulk copy per expert) stream into shared memory together with the
+//     gate/up rows.  Every CTA polls the a2 words of all the union's neurons until they carry
+//     this launch's epoch (no flag, fence or atomic on the critical path), then
+//     out[h] = bf16(sum over experts, neurons of a2 * down_t[e][h][j]) in a fixed order, written
+//     straight to the output: no cross-CTA reduction of outputs.  Experts beyond the shared
+//     memory budget are processed in chunks (one a2 exchange each).
+//  The epoch word is advanced by CTA 0 after it has seen every CTA's presence word of this
+//  launch (each CTA writes one right after reading the epoch).  The polls need every CTA of
+//  the grid resident: the grid is one CTA per SM (two fit), and with programmatic dependent
+//  launch a grid is only launched after every CTA of its predecessor is running.
 //
 // Rounding points: logit = bf16(x.R) (+ bias, bf16); g,u -> bf16; s = bf16(silu(g));
-// a = bf16(s u); a2 = bf16(a w); out = bf16(sum a2 Wd).  Every wait is bounded and records
-// a status bit instead of hanging.
+// a = bf16(s u); a2 = bf16(a w); out = bf16(sum a2 Wd).  Deterministic (fixed summation
+// orders).  Every wait is bounded and records a status bit instead of hanging.
 #include <cooperative_groups.h>
 #include "common.cuh"
 #include "select.cuh"
@@ -45,14 +49,15 @@ namespace ppmoe {
 
 constexpr int kD1Threads = 384;
 constexpr int kD1Warps = kD1Threads / 32;
-constexpr int kD1MaxHCH = 3;        // float4 column units per thread: H <= 4 * 384 * 3
-constexpr int kD1TileBars = 12;     // tile barriers (slots <= 48)
-constexpr int kD1MaxGrid = 160;     // partial rows in the workspace region
+constexpr int kD1MaxSlots = 24;     // gate/up slots (one mbarrier each)
+constexpr int kD1MaxXI = 8;         // 16-byte token chunks per lane: H <= 2048
+constexpr int kD1MaxGrid = 160;     // presence words in the workspace region
 
 struct D1Args {
   const __nv_bfloat16* x;
   const __nv_bfloat16* router_eh;  // [E][H]
   const __nv_bfloat16* experts;    // [E][G][3][H]
+  const __nv_bfloat16* down_t;     // [E][H][G]
   int H, E, G;
   float tau_b;
   const float* bias;
@@ -60,12 +65,15 @@ struct D1Args {
   __nv_bfloat16* logits_out;
   __nv_bfloat16* weights_out;
   long long* counts;
-  unsigned long long* part;  // [H / 4][grid][4] tagged fp32 CTA partials (unit-major)
-  uint32_t* epoch;           // launch epoch (advanced by CTA 0 at its end)
+  unsigned long long* a2x;       // [E G] tagged a2 of the union's neurons (union order)
+  unsigned long long* presence;  // [grid] tagged presence words
+  uint32_t* epoch;               // launch epoch (advanced by CTA 0 at its end)
   uint32_t* status;
-  int slots;
+  int CE;     // experts per chunk
+  int S;      // gate/up slots (>= neurons of one CTA in one chunk)
+  int NC;     // >= hidden columns of one CTA
+  int trig_early;             // signal dependents at the start (1) or after the selection (0)
   int pdl;
-  int trig_early;     // signal dependents at the start (1) or after the selection (0)
   unsigned long long* trace;  // optional [grid][32] globaltimer stamps (diagnostics)
 };
 
@@ -82,12 +90,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_relaxed_v2u64(unsigned long long* p, unsigned long long a, unsigned long long b) {
-  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ void ld_relaxed_v2u64(const unsigned long long* p, unsigned long long& a,
-                                                 unsigned long long& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 // 4-byte store into a peer CTA's shared memory that completes 4 transaction bytes on the
 // peer's mbarrier (both addresses shared::cluster)
@@ -95,25 +104,32 @@ __device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t ba
   asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
                ::"r"(addr), "r"(__float_as_uint(v)), "r"(bar) : "memory");
 }
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 struct D1Smem {
-  uint32_t bars, x, lg, w, ulist, misc, scr, ring, total;
+  uint32_t bars, x, lg, w, ulist, misc, scr, alias, a2s, dred, dsl, ring, total;
 };
 
-__host__ __device__ inline uint32_t d1_slot_bytes(int H) { return 6u * (uint32_t)H + 32u; }
+__host__ __device__ inline uint32_t d1_slot_bytes(int H) { return 4u * (uint32_t)H + 32u; }
 __host__ __device__ inline uint32_t d1_router_pitch(int H) { return 2u * (uint32_t)H + 32u; }
 
-__host__ __device__ inline D1Smem d1_smem(int H, int E, int slots) {
+__host__ __device__ inline D1Smem d1_smem(int H, int E, int G, int CE, int S, int NC) {
   D1Smem s;
   uint32_t o = 0;
-  s.bars = o;  o += 8 * 16;
+  s.bars = o;  o += 8 * 32;
   s.x = o;     o = (uint32_t)align_up(o + 2 * (size_t)H + 16, 128);
   s.lg = o;    o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.w = o;     o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.ulist = o; o = (uint32_t)align_up(o + (size_t)E * 4, 128);
   s.misc = o;  o = (uint32_t)align_up(o + 64, 128);
-  s.scr = o;   o = (uint32_t)align_up(o + 3072 + 512, 1024);  // selection scratch | router / gate-up parts, a2
-  s.ring = o;  o += (uint32_t)slots * d1_slot_bytes(H);
+  s.scr = o;   o = (uint32_t)align_up(o + 3072 + 512, 1024);  // selection scratch | router warp parts
+  // from here on the region also holds the router rows until the selection is done
+  s.alias = o;
+  s.a2s = o;   o = (uint32_t)align_up(o + (size_t)CE * G * 4, 128);
+  s.dred = o;  o = (uint32_t)align_up(o + (size_t)NC * CE * 4, 128);
+  s.dsl = o;   o = (uint32_t)align_up(o + (size_t)CE * NC * G * 2, 128);
+  s.ring = o;  o += (uint32_t)S * d1_slot_bytes(H);
   s.total = o;
   return s;
 }
@@ -124,24 +140,30 @@ __global__ void __launch_bounds__(kD1Threads, 2) decode1_kernel(const D1Args a) 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rank = (int)cluster.block_rank();
   const int H = a.H, E = a.E, G = a.G, EH = a.E >> 1;
-  const D1Smem L = d1_smem(H, E, a.slots);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  uint64_t* bar_in = bars + kD1TileBars;      // this rank's router rows
-  uint64_t* bar_lg = bars + kD1TileBars + 1;  // the peer's E/2 logits (st.async bytes)
+  const int P = gridDim.x, bid = blockIdx.x;
+  const D1Smem L = d1_smem(H, E, G, a.CE, a.S, a.NC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);  // [0, S): gate/up slots
+  uint64_t* bar_dsl = bars + kD1MaxSlots;
+  uint64_t* bar_in = bars + kD1MaxSlots + 1;  // this rank's router rows
+  uint64_t* bar_lg = bars + kD1MaxSlots + 2;  // the peer's E/2 logits (st.async bytes)
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + L.x);
   float* lg = reinterpret_cast<float*>(smem + L.lg);
   float* ws = reinterpret_cast<float*>(smem + L.w);
   int* ulist = reinterpret_cast<int*>(smem + L.ulist);
   int* misc = reinterpret_cast<int*>(smem + L.misc);  // [0] |U|, [1] epoch
   float* scr = reinterpret_cast<float*>(smem + L.scr);
+  float* a2s = reinterpret_cast<float*>(smem + L.a2s);
+  float* dred = reinterpret_cast<float*>(smem + L.dred);
+  uint8_t* dsl = smem + L.dsl;
   uint8_t* ring = smem + L.ring;
+  uint8_t* rrows = smem + L.alias;
   const uint32_t hb = 2u * (uint32_t)H, rpitch = d1_router_pitch(H), slotb = d1_slot_bytes(H);
-  const uint32_t rec = 3u * hb;
   const int g8 = lane >> 2, q = lane & 3;
 
   D1_TRACE(0);
   if (tid == 0) {
-    for (int s = 0; s < kD1TileBars; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kD1MaxSlots; ++s) mbar_init(&bars[s], 1);
+    mbar_init(bar_dsl, 1);
     mbar_init(bar_in, 1);
     mbar_init(bar_lg, 1);
     fence_mbar_init();
@@ -155,7 +177,7 @@ __global__ void __launch_bounds__(kD1Threads, 2) decode1_kernel(const D1Args a) 
     __syncwarp();
     const uint64_t pol = policy_evict_last();
     for (int e = lane; e < EH; e += 32)
-      bulk_g2s(ring + (size_t)e * rpitch, a.router_eh + (size_t)(rank * EH + e) * H, hb, bar_in, pol);
+      bulk_g2s(rrows + (size_t)e * rpitch, a.router_eh + (size_t)(rank * EH + e) * H, hb, bar_in, pol);
   }
   if (a.trig_early) pdl_launch_dependents();
   if (a.pdl) pdl_wait();
@@ -163,52 +185,64 @@ __global__ void __launch_bounds__(kD1Threads, 2) decode1_kernel(const D1Args a) 
   // token row: plain 16-byte loads (written by the previous kernel, normally still in L2)
   for (int i = tid; i < H / 8; i += kD1Threads)
     reinterpret_cast<uint4*>(xs)[i] = reinterpret_cast<const uint4*>(a.x)[i];
-  if (tid == 0) misc[1] = (int)(ld_acquire_gpu(a.epoch) + 1u);
+  if (tid == 0) {
+    const uint32_t ep = ld_acquire_gpu(a.epoch) + 1u;
+    misc[1] = (int)ep;
+    st_relaxed_u64(a.presence + bid, (unsigned long long)ep << 32);
+  }
   mbar_wait(bar_in, 0u, a.status);
   __syncthreads();
   D1_TRACE(2);
 
   // ---- 1. router on the tensor cores: D[16 x 8] += A[16 x 16] B[16 x 8] per k-step and
   // expert tile; A row 0 = the token (lanes 0-3), B column n = router row of expert 8t + n.
-  // Warp w takes k-steps [w KS / 12, (w+1) KS / 12) of every tile.
+  // Warp w takes k-steps [w KS / 12, (w+1) KS / 12) of every tile; all tiles and both k
+  // parities accumulate in independent chains.
   {
-    const int KS = H >> 4, NTL = (EH + 7) >> 3;
+    const int KS = H >> 4, NTL = (EH + 7) >> 3;  // NTL <= 4 (E <= 64)
     const int k0 = (KS * warp) / kD1Warps, k1 = (KS * (warp + 1)) / kD1Warps;
     float* rpart = scr;  // [12][EH]
     const uint32_t xrow = smem_u32(xs) + 8 * q;
+    uint32_t brow[4];
+    float d[4][2][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      brow[t] = smem_u32(rrows + (size_t)min(8 * t + g8, EH - 1) * rpitch) + 8 * q;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) d[t][h][0] = d[t][h][1] = d[t][h][2] = d[t][h][3] = 0.f;
+    }
     #pragma unroll 1
-    for (int t = 0; t < NTL; ++t) {
-      const uint32_t brow = smem_u32(ring + (size_t)min(8 * t + g8, EH - 1) * rpitch) + 8 * q;
-      float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      #pragma unroll 2
-      for (int k = k0; k < k1; k += 2) {  // two independent accumulators
-        uint2 bv[2], xa[2];
+    for (int k = k0; k < k1; k += 2) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int kk = min(k + h, k1 - 1);
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv[h].x), "=r"(bv[h].y) : "r"(brow + 32 * kk));
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(xa[h].x), "=r"(xa[h].y) : "r"(xrow + 32 * kk));
-          if (lane >= 4 || k + h >= k1) xa[h] = make_uint2(0u, 0u);
+      for (int h = 0; h < 2; ++h) {
+        const int kk = min(k + h, k1 - 1);
+        uint2 xa;
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(xa.x), "=r"(xa.y) : "r"(xrow + 32 * kk));
+        if (lane >= 4 || k + h >= k1) xa = make_uint2(0u, 0u);  // only A row 0 carries the token
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if (t < NTL) {
+            uint2 bv;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv.x), "=r"(bv.y) : "r"(brow[t] + 32 * kk));
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+f"(d[t][h][0]), "+f"(d[t][h][1]), "+f"(d[t][h][2]), "+f"(d[t][h][3])
+                : "r"(xa.x), "r"(0u), "r"(xa.y), "r"(0u), "r"(bv.x), "r"(bv.y));
+          }
         }
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(d[h][0]), "+f"(d[h][1]), "+f"(d[h][2]), "+f"(d[h][3])
-              : "r"(xa[h].x), "r"(0u), "r"(xa[h].y), "r"(0u), "r"(bv[h].x), "r"(bv[h].y));
-      }
-      if (lane < 4) {
-        const int e = 8 * t + 2 * q;
-        if (e < EH) rpart[warp * EH + e] = d[0][0] + d[1][0];
-        if (e + 1 < EH) rpart[warp * EH + e + 1] = d[0][1] + d[1][1];
       }
     }
-    D1_TRACE(11);
+    if (lane < 4) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int e = 8 * t + 2 * q;
+        if (e < EH) rpart[warp * EH + e] = d[t][0][0] + d[t][1][0];
+        if (e + 1 < EH) rpart[warp * EH + e + 1] = d[t][0][1] + d[t][1][1];
+      }
+    }
     __syncthreads();
-    D1_TRACE(12);
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-    D1_TRACE(13);
     if (tid < EH) {  // thread e: this rank's logit of expert rank EH + e, here and at the peer
       float s = 0.f;
 #pragma unroll
@@ -219,7 +253,6 @@ __global__ void __launch_bounds__(kD1Threads, 2) decode1_kernel(const D1Args a) 
       st_async_f32(mapa_u32(lg + rank * EH + tid, (uint32_t)(rank ^ 1)), l, mapa_u32(bar_lg, (uint32_t)(rank ^ 1)));
     }
   }
-  D1_TRACE(14);
   __syncthreads();                    // this rank's half of lg
   mbar_wait(bar_lg, 0u, a.status);    // the peer's half
   D1_TRACE(3);
@@ -246,215 +279,179 @@ __global__ void __launch_bounds__(kD1Threads, 2) decode1_kernel(const D1Args a) 
   D1_TRACE(4);
   if (!a.trig_early) pdl_launch_dependents();
 
-  // ---- 3. experts: this CTA's neurons [i0, i0 + cnt) of the union's |U| G
-  const int S = a.slots;
-  const uint32_t Wn = (uint32_t)misc[0] * (uint32_t)G;  // <= 256 * 256
-  const int i0 = (int)(Wn * blockIdx.x / gridDim.x);
-  const int cnt = (int)(Wn * (blockIdx.x + 1) / gridDim.x) - i0;
-  const int rounds = (cnt + S - 1) / S;
+  // ---- 3 + 4, per chunk of CE experts of the union
+  const int nU = misc[0];
+  const uint32_t want = (uint32_t)misc[1];
+  const unsigned long long ep = (unsigned long long)want << 32;
+  const int h0 = (int)((uint32_t)H * bid / P), ncols = (int)((uint32_t)H * (bid + 1) / P) - h0;
+  const int NX = H >> 3;  // 16-byte token chunks; lane covers chunks lane + 32 i
   const uint64_t pol = policy_evict_first();
-  // round r: neurons [r S, r S + nr) into slots 0..nr-1; tile t (slots 4t..4t+3) completes on
-  // bars[t].  Lane 0 of warp w arms tile w and issues neurons w, w + 12, ... (copies issued by
-  // one thread are serialised, so the issue is spread over the warps).
-  auto issue = [&](int r) {
-    const int nb = r * S, nr = min(S, cnt - nb);
-    if (lane == 0) {
-      if (warp < (nr + 3) / 4) mbar_arrive_expect_tx(&bars[warp], (uint32_t)min(4, nr - 4 * warp) * rec);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int n = warp; n < nr; n += kD1Warps) {
-        const int gi = i0 + nb + n, u = gi / G;
-        bulk_g2s(ring + (size_t)n * slotb, a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H, rec,
-                 &bars[n >> 2], pol);
-      }
-    }
-  };
-  if (cnt > 0) issue(0);
-  D1_TRACE(5);
-  // optional side outputs from the first CTA (off the critical path of the others)
-  if (blockIdx.x == 0) {
-    for (int e = tid; e < E; e += kD1Threads) {
-      if (a.logits_out) a.logits_out[e] = __float2bfloat16_rn(lg[e]);
-      if (a.weights_out) a.weights_out[e] = __float2bfloat16_rn(ws[e]);
-      if (a.counts && ws[e] > 0.f) a.counts[e] += 1;
-    }
-  }
-
-  float acc[kD1MaxHCH][4];
-#pragma unroll
-  for (int c = 0; c < kD1MaxHCH; ++c) acc[c][0] = acc[c][1] = acc[c][2] = acc[c][3] = 0.f;
-  const int ksteps = H >> 4;
+  float accv = 0.f;  // thread tid < ncols: output column h0 + tid
+  const int nch = (nU + a.CE - 1) / a.CE;
   #pragma unroll 1
-  for (int r = 0; r < rounds; ++r) {
-    const int nb = r * S, nr = min(S, cnt - nb);
-    if (r > 0) {
-      __syncthreads();  // every slot of the previous round is consumed
-      issue(r);
-    }
-    // gate/up: warp w takes tile w % T and k-part w / T of KS = 12 / T parts
-    const int T = (nr + 3) >> 2;
-    const int KS = kD1Warps / T;
-    const int tile = warp % T, kpi = warp / T;
-    float* kpart = scr;  // [KS][T][8]
-    if (kpi < KS) {
-      const int k0 = (ksteps * kpi) / KS, k1 = (ksteps * (kpi + 1)) / KS;
-      const int nrow = min(4 * tile + (g8 >> 1), nr - 1);  // padding columns read a valid row
-      const uint32_t brow = smem_u32(ring + (size_t)nrow * slotb + (g8 & 1) * hb) + 8 * q;
-      const uint32_t xrow = smem_u32(xs) + 8 * q;
-      float d[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) d[i][0] = d[i][1] = d[i][2] = d[i][3] = 0.f;
-      mbar_wait(&bars[tile], (uint32_t)(r & 1), a.status);
-      if (r == 0 && warp == 0) D1_TRACE(6);
-      #pragma unroll 1
-      for (int kk = k0; kk < k1; kk += 4) {
-        uint2 xa[4], bv[4];
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2) {
-          const int k = min(kk + s2, k1 - 1);
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(bv[s2].x), "=r"(bv[s2].y) : "r"(brow + 32 * k));
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(xa[s2].x), "=r"(xa[s2].y) : "r"(xrow + 32 * k));
-          // only A row 0 (lanes 0-3) carries the token; steps past k1 contribute nothing
-          if (lane >= 4 || kk + s2 >= k1) xa[s2] = make_uint2(0u, 0u);
-        }
-#pragma unroll
-        for (int s2 = 0; s2 < 4; ++s2)
-          asm volatile(
-              "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-              "{%0,%1,%2,%3};"
-              : "+f"(d[s2][0]), "+f"(d[s2][1]), "+f"(d[s2][2]), "+f"(d[s2][3])
-              : "r"(xa[s2].x), "r"(0u), "r"(xa[s2].y), "r"(0u), "r"(bv[s2].x), "r"(bv[s2].y));
+  for (int ch = 0; ch < nch; ++ch) {
+    const int eb = ch * a.CE, nUc = min(a.CE, nU - eb);
+    const uint32_t nb = (uint32_t)eb * G, Wc = (uint32_t)nUc * G;
+    const int i0 = (int)(nb + Wc * bid / P), cnt = (int)(nb + Wc * (bid + 1) / P) - i0;
+    const uint32_t par = (uint32_t)(ch & 1);
+    if (ch > 0) __syncthreads();  // the previous chunk's slots, down rows and a2 are consumed
+    // issue: lane 0 of warp w copies gate/up slots w, w + 12, ... and the down rows of chunk
+    // experts w, w + 12, ... (copies issued by one thread are serialised)
+    if (lane == 0) {
+      if (warp == 0) mbar_arrive_expect_tx(bar_dsl, (uint32_t)nUc * ncols * G * 2);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int s = warp; s < cnt; s += kD1Warps) {
+        const int gi = i0 + s, u = gi / G;
+        mbar_arrive_expect_tx(&bars[s], 2u * hb);
+        bulk_g2s(ring + (size_t)s * slotb, a.experts + ((size_t)ulist[u] * G + (gi - u * G)) * 3 * H, 2u * hb,
+                 &bars[s], pol);
       }
-      if (lane < 4) {
-        kpart[(kpi * T + tile) * 8 + 2 * q] = (d[0][0] + d[1][0]) + (d[2][0] + d[3][0]);      // gate
-        kpart[(kpi * T + tile) * 8 + 2 * q + 1] = (d[0][1] + d[1][1]) + (d[2][1] + d[3][1]);  // up
-      }
+      for (int ei = warp; ei < nUc; ei += kD1Warps)
+        bulk_g2s(dsl + (size_t)ei * a.NC * G * 2, a.down_t + ((size_t)ulist[eb + ei] * H + h0) * G,
+                 (uint32_t)ncols * G * 2, bar_dsl, pol);
     }
-    __syncthreads();
-    float* a2k = scr + kD1Warps * 8 * 2;
-    if (tid < nr) {
-      float g = 0.f, uu = 0.f;
-      #pragma unroll 1
-      for (int p = 0; p < KS; ++p) {  // part order
-        const int o = (p * T + (tid >> 2)) * 8 + 2 * (tid & 3);
-        g += kpart[o];
-        uu += kpart[o + 1];
-      }
-      const float gb = bf16r(g), ub = bf16r(uu);
-      const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
-      a2k[tid] = bf16r(bf16r(sb * ub) * ws[ulist[(i0 + nb + tid) / G]]);
-    }
-    __syncthreads();
-    if (r == 0) D1_TRACE(7);
-    // down rows: thread tid owns hidden columns 4 h4 .. 4 h4 + 3, h4 = tid + 384 c
-#pragma unroll
-    for (int c = 0; c < kD1MaxHCH; ++c) {
-      const int h4 = tid + c * kD1Threads;
-      if (h4 < H / 4) {
-        #pragma unroll 1
-        for (int m0 = 0; m0 < nr; m0 += 4) {
-          uint2 dv[4];
-          float av[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int m = min(m0 + i, nr - 1);
-            dv[i] = *reinterpret_cast<const uint2*>(ring + (size_t)m * slotb + 2 * hb + 8 * h4);
-            av[i] = m0 + i < nr ? a2k[m0 + i] : 0.f;  // 0 * finite weight adds exactly nothing
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 d01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[i].x));
-            const float2 d23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv[i].y));
-            acc[c][0] = fmaf(av[i], d01.x, acc[c][0]);
-            acc[c][1] = fmaf(av[i], d01.y, acc[c][1]);
-            acc[c][2] = fmaf(av[i], d23.x, acc[c][2]);
-            acc[c][3] = fmaf(av[i], d23.y, acc[c][3]);
-          }
+    if (ch == 0) {
+      D1_TRACE(5);
+      if (bid == 0) {  // optional side outputs from the first CTA
+        for (int e = tid; e < E; e += kD1Threads) {
+          if (a.logits_out) a.logits_out[e] = __float2bfloat16_rn(lg[e]);
+          if (a.weights_out) a.weights_out[e] = __float2bfloat16_rn(ws[e]);
+          if (a.counts && ws[e] > 0.f) a.counts[e] += 1;
         }
       }
     }
-  }
-  D1_TRACE(8);
-
-  // ---- 4. grid reduction over epoch-tagged partials
-  const unsigned long long ep = (unsigned long long)(uint32_t)misc[1] << 32;
-  {
-    // unit-major: a consumer's entries (its units x every partial) are contiguous
+    // gate/up: warp w takes slots w, w + 12, ...; lanes split K, butterfly sums (fixed order)
+    #pragma unroll 1
+    for (int s = warp; s < cnt; s += kD1Warps) {
+      mbar_wait(&bars[s], par, a.status);
+      if (ch == 0 && s == 0) D1_TRACE(6);
+      const uint4* gr = reinterpret_cast<const uint4*>(ring + (size_t)s * slotb);
+      const uint4* ur = reinterpret_cast<const uint4*>(ring + (size_t)s * slotb + hb);
+      float g0 = 0.f, g1 = 0.f, u0 = 0.f, u1 = 0.f;
 #pragma unroll
-    for (int c = 0; c < kD1MaxHCH; ++c) {
-      const int h4 = tid + c * kD1Threads;
-      if (h4 < H / 4) {
-        unsigned long long* dst = a.part + ((size_t)h4 * gridDim.x + blockIdx.x) * 4;
-        st_relaxed_v2u64(dst, ep | __float_as_uint(acc[c][0]), ep | __float_as_uint(acc[c][1]));
-        st_relaxed_v2u64(dst + 2, ep | __float_as_uint(acc[c][2]), ep | __float_as_uint(acc[c][3]));
-      }
-    }
-  }
-  D1_TRACE(9);
-  {
-    const int U = H >> 2, P = gridDim.x;
-    const int u0 = (int)((uint32_t)U * blockIdx.x / (uint32_t)P);
-    const int nu = (int)((uint32_t)U * (blockIdx.x + 1) / (uint32_t)P) - u0;
-    float4* red = reinterpret_cast<float4*>(ring);  // [nu][P]; the ring is idle
-    __syncthreads();  // every warp is done with the ring
-    // entries (unit j, partial p); each thread polls its entries until all 4 words carry
-    // this launch's epoch
-    const uint32_t want = (uint32_t)(ep >> 32);
-    for (int i = tid; i < nu * P; i += kD1Threads) {
-      const unsigned long long* src = a.part + ((size_t)u0 * P + i) * 4;  // entry (u0 + i / P, i % P)
-      unsigned long long w0, w1, w2, w3;
-      uint32_t it = 0;
-      #pragma unroll 1
-      for (;;) {
-        ld_relaxed_v2u64(src, w0, w1);
-        ld_relaxed_v2u64(src + 2, w2, w3);
-        if ((uint32_t)(w0 >> 32) == want && (uint32_t)(w1 >> 32) == want && (uint32_t)(w2 >> 32) == want &&
-            (uint32_t)(w3 >> 32) == want)
-          break;
-        if (++it > kSpinLimit) {
-          atomicOr(a.status, DEVERR_TIMEOUT);
-          break;
+      for (int i = 0; i < kD1MaxXI; ++i) {
+        const int c = lane + 32 * i;
+        if (c < NX) {
+          const uint4 gv = gr[c], uv = ur[c], xv = reinterpret_cast<const uint4*>(xs)[c];
+          g0 = fmaf(bf_lo(xv.x), bf_lo(gv.x), g0); g1 = fmaf(bf_hi(xv.x), bf_hi(gv.x), g1);
+          g0 = fmaf(bf_lo(xv.y), bf_lo(gv.y), g0); g1 = fmaf(bf_hi(xv.y), bf_hi(gv.y), g1);
+          g0 = fmaf(bf_lo(xv.z), bf_lo(gv.z), g0); g1 = fmaf(bf_hi(xv.z), bf_hi(gv.z), g1);
+          g0 = fmaf(bf_lo(xv.w), bf_lo(gv.w), g0); g1 = fmaf(bf_hi(xv.w), bf_hi(gv.w), g1);
+          u0 = fmaf(bf_lo(xv.x), bf_lo(uv.x), u0); u1 = fmaf(bf_hi(xv.x), bf_hi(uv.x), u1);
+          u0 = fmaf(bf_lo(xv.y), bf_lo(uv.y), u0); u1 = fmaf(bf_hi(xv.y), bf_hi(uv.y), u1);
+          u0 = fmaf(bf_lo(xv.z), bf_lo(uv.z), u0); u1 = fmaf(bf_hi(xv.z), bf_hi(uv.z), u1);
+          u0 = fmaf(bf_lo(xv.w), bf_lo(uv.w), u0); u1 = fmaf(bf_hi(xv.w), bf_hi(uv.w), u1);
         }
-        __nanosleep(100);  // back off: early finishers must not crowd out the last CTAs' traffic
       }
-      red[i] = make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1),
-                           __uint_as_float((uint32_t)w2), __uint_as_float((uint32_t)w3));
-    }
-    D1_TRACE(18);
-    __syncthreads();
-    D1_TRACE(19);
-    for (int j = warp; j < nu; j += kD1Warps) {
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int p = lane; p < P; p += 32) {
-        const float4 v = red[j * P + p];
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
-      }
+      float g = g0 + g1, uu = u0 + u1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {  // fixed tree; lane 0's sum is reproducible
-        s.x += __shfl_xor_sync(0xffffffffu, s.x, o);
-        s.y += __shfl_xor_sync(0xffffffffu, s.y, o);
-        s.z += __shfl_xor_sync(0xffffffffu, s.z, o);
-        s.w += __shfl_xor_sync(0xffffffffu, s.w, o);
+      for (int o = 16; o > 0; o >>= 1) {
+        g += __shfl_xor_sync(0xffffffffu, g, o);
+        uu += __shfl_xor_sync(0xffffffffu, uu, o);
       }
       if (lane == 0) {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
-        uint2 pk;
-        pk.x = *reinterpret_cast<uint32_t*>(&lo);
-        pk.y = *reinterpret_cast<uint32_t*>(&hi);
-        *reinterpret_cast<uint2*>(a.out + 4 * (size_t)(u0 + j)) = pk;
+        const int gi = i0 + s;
+        const float gb = bf16r(g), ub = bf16r(uu);
+        const float sb = bf16r(__fmul_rn(gb, __frcp_rn(1.f + expf(-gb))));  // silu
+        const float a2 = bf16r(bf16r(sb * ub) * ws[ulist[gi / G]]);
+        st_relaxed_u64(a.a2x + gi, ep | __float_as_uint(a2));
       }
     }
+    if (ch == 0) D1_TRACE(7);
+    if (a.trace) {  // diagnostics only: when every warp of the CTA is done with gate/up
+      __syncthreads();
+      if (ch == 0) D1_TRACE(16);
+    }
+    // every a2 of the chunk (and, in CTA 0's last chunk, every CTA's presence word) polled
+    // until it carries this launch's epoch; four entries per thread in flight
+    {
+      const int n = (int)Wc + ((bid == 0 && ch == nch - 1) ? P : 0);
+      #pragma unroll 1
+      for (int b = 0; b < n; b += 4 * kD1Threads) {
+        unsigned long long v[4];
+        bool rdy[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          rdy[k] = b + tid + k * kD1Threads >= n;
+          v[k] = 0ull;
+        }
+        uint32_t it = 0;
+        #pragma unroll 1
+        for (;;) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int idx = b + tid + k * kD1Threads;
+            if (!rdy[k]) v[k] = ld_relaxed_u64(idx < (int)Wc ? a.a2x + nb + idx : a.presence + (idx - (int)Wc));
+          }
+          bool all = true;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            rdy[k] = rdy[k] || (uint32_t)(v[k] >> 32) == want;
+            all = all && rdy[k];
+          }
+          if (all) break;
+          if (++it > kSpinLimit) {
+            atomicOr(a.status, DEVERR_TIMEOUT);
+            break;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int idx = b + tid + k * kD1Threads;
+          if (idx < (int)Wc) a2s[idx] = __uint_as_float((uint32_t)v[k]);
+        }
+      }
+    }
+    if (ch == 0) D1_TRACE(11);
+    __syncthreads();
+    if (ch == 0) D1_TRACE(8);
+    mbar_wait(bar_dsl, par, a.status);
+    if (ch == 0) D1_TRACE(12);
+    // down: thread t -> (column t % ncols, chunk expert t / ncols), a G-long dot product read in
+    // a rotated order (spreads the rows of neighbouring threads over the banks)
+    {
+      const int G8 = G >> 3;
+      for (int t = tid; t < ncols * nUc; t += kD1Threads) {
+        const int col = t % ncols, ei = t / ncols;
+        const uint4* row = reinterpret_cast<const uint4*>(dsl + ((size_t)ei * a.NC + col) * G * 2);
+        const float* av = a2s + ei * G;
+        float s0 = 0.f, s1 = 0.f;
+        int kk = t % G8;
+        #pragma unroll 4
+        for (int i = 0; i < G8; ++i) {
+          const uint4 dv = row[kk];
+          const float4 a0 = *reinterpret_cast<const float4*>(av + 8 * kk);
+          const float4 a1 = *reinterpret_cast<const float4*>(av + 8 * kk + 4);
+          s0 = fmaf(a0.x, bf_lo(dv.x), s0); s1 = fmaf(a0.y, bf_hi(dv.x), s1);
+          s0 = fmaf(a0.z, bf_lo(dv.y), s0); s1 = fmaf(a0.w, bf_hi(dv.y), s1);
+          s0 = fmaf(a1.x, bf_lo(dv.z), s0); s1 = fmaf(a1.y, bf_hi(dv.z), s1);
+          s0 = fmaf(a1.z, bf_lo(dv.w), s0); s1 = fmaf(a1.w, bf_hi(dv.w), s1);
+          kk = kk + 1 == G8 ? 0 : kk + 1;
+        }
+        dred[col * a.CE + ei] = s0 + s1;
+      }
+    }
+    if (ch == 0) D1_TRACE(13);
+    __syncthreads();
+    if (ch == 0) D1_TRACE(14);
+    if (tid < ncols) {
+      float s = 0.f;
+      for (int ei = 0; ei < nUc; ++ei) s += dred[tid * a.CE + ei];  // expert order
+      accv += s;
+    }
   }
-  // CTA 0 has seen every CTA's partial of this launch, so every CTA has read the epoch
-  if (blockIdx.x == 0 && tid == 0)
-    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.epoch), "r"((uint32_t)(ep >> 32)) : "memory");
+  if (tid < ncols) a.out[h0 + tid] = __float2bfloat16_rn(accv);
+  // CTA 0 has seen every CTA's presence word of this launch: every CTA has read the epoch
+  if (bid == 0 && tid == 0)
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(a.epoch), "r"(want) : "memory");
   D1_TRACE(10);
-  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 30] = (unsigned long long)cnt;
+  if (a.trace && tid == 0) a.trace[blockIdx.x * 32 + 30] = (unsigned long long)nch;
 }
 
 // ------------------------------------------------------------------ host side
 struct D1Cfg {
-  int dev = -1, H = 0, E = 0;
-  int ok = 0, slots = 0, grid = 0;
+  int dev = -1, H = 0, E = 0, G = 0;
+  int ok = 0, grid = 0, CE = 0, S = 0, NC = 0;
   uint32_t smem = 0;
 };
 static thread_local D1Cfg g_d1;
@@ -468,36 +465,43 @@ static int d1_mode() {
   return g_d1_mode;
 }
 
-// Bytes of the tagged-partial region the single-token kernel needs for hidden size H.
-size_t decode1_region_bytes(int H) { return (size_t)kD1MaxGrid * H * 8; }
+// Bytes of the workspace region the single-token kernel needs: tagged a2 of every neuron and
+// one presence word per CTA.
+size_t decode1_region_bytes(int E, int G) { return ((size_t)E * G + kD1MaxGrid) * 8; }
 
 // Returns 1 if launched, 0 if the kernel does not apply (caller falls back), < 0 on error.
-// part: the tagged-partial region (decode1_region_bytes); epoch: a word that only this kernel
-// writes (zero-initialised with the workspace).
+// region: decode1_region_bytes; epoch: a word that only this kernel writes (zero-initialised
+// with the workspace, like the region).
 int decode1_launch(const void* x, const void* packed, int H, int E, int G, float tau, const float* bias, void* out,
                    void* logits_out, void* weights_out, int64_t* counts, int pdl, cudaStream_t stream,
-                   uint32_t* status, uint32_t* epoch, void* part, size_t part_bytes, unsigned long long* trace) {
+                   uint32_t* status, uint32_t* epoch, void* region, size_t region_bytes,
+                   unsigned long long* trace) {
   const int mode = d1_mode();
-  if (mode == 0 || E > 64 || (E & 1) || H % 64 != 0 || H > 4 * kD1Threads * kD1MaxHCH || !part) return 0;
+  if (mode == 0 || E > 64 || (E & 1) || H % 64 != 0 || H > 256 * kD1MaxXI || G % 8 != 0 || !region ||
+      region_bytes < decode1_region_bytes(E, G))
+    return 0;
   int dev = 0;
   PPMOE_CHECK_CUDA(cudaGetDevice(&dev));
   D1Cfg& C = g_d1;
-  if (C.dev != dev || C.H != H || C.E != E) {
+  if (C.dev != dev || C.H != H || C.E != E || C.G != G) {
     C = D1Cfg();
-    C.dev = dev; C.H = H; C.E = E;
+    C.dev = dev; C.H = H; C.E = E; C.G = G;
     int nsm = 0, smem_sm = 0;
     PPMOE_CHECK_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
     PPMOE_CHECK_CUDA(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
     // two CTAs per SM: each gets half the SM's shared memory minus the per-CTA reservation
     const int budget = smem_sm / 2 - 1024 - 1024;  // -1024: alignment slack of the dynamic base
-    int slots = 4 * kD1TileBars;  // tiles of 4 neurons <= warps
-    while (slots > 1 && (int)d1_smem(H, E, slots).total > budget) --slots;
-    const D1Smem Lm = d1_smem(H, E, slots);
-    const size_t ring = (size_t)slots * d1_slot_bytes(H);
-    const size_t router_need = (size_t)(E / 2) * d1_router_pitch(H);
     const int grid = (nsm / 2) * 2;
-    const size_t red_need = (size_t)((H / 4 + grid - 1) / grid) * grid * 16;
-    if (slots >= 4 && (int)Lm.total <= budget && router_need <= ring && red_need <= ring && grid <= kD1MaxGrid) {
+    const int NC = (H + grid - 1) / grid;
+    int CE = E, S = 0;
+    D1Smem Lm{};
+    for (; CE >= 1; --CE) {
+      S = (CE * G + grid - 1) / grid;
+      Lm = d1_smem(H, E, G, CE, S, NC);
+      if (S <= kD1MaxSlots && (int)Lm.total <= budget) break;
+    }
+    const size_t router_need = (size_t)(E / 2) * d1_router_pitch(H);
+    if (CE >= 1 && grid <= kD1MaxGrid && router_need <= Lm.total - Lm.alias) {
       const uint32_t smem = Lm.total + 1024;
       PPMOE_CHECK_CUDA(cudaFuncSetAttribute(decode1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       cudaLaunchConfig_t cfg = {};
@@ -513,21 +517,24 @@ int decode1_launch(const void* x, const void* packed, int H, int E, int G, float
       cfg.numAttrs = 1;
       int clusters = 0;
       PPMOE_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&clusters, decode1_kernel, &cfg));
-      // the partial polls need the whole grid resident
-      if (clusters * 2 >= grid) {
+      if (clusters * 2 >= grid) {  // the a2 polls need the whole grid resident
         C.ok = 1;
-        C.slots = slots;
         C.grid = grid;
+        C.CE = CE;
+        C.S = S;
+        C.NC = NC;
         C.smem = smem;
       }
     }
   }
-  if (!C.ok || (size_t)C.grid * H * 8 > part_bytes) return 0;
+  if (!C.ok) return 0;
   const PackedLayout PL = packed_layout(H, E, G);
+  const uint8_t* pk = static_cast<const uint8_t*>(packed);
   D1Args a;
   a.x = static_cast<const __nv_bfloat16*>(x);
-  a.router_eh = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.router_eh);
-  a.experts = reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(packed) + PL.experts);
+  a.router_eh = reinterpret_cast<const __nv_bfloat16*>(pk + PL.router_eh);
+  a.experts = reinterpret_cast<const __nv_bfloat16*>(pk + PL.experts);
+  a.down_t = reinterpret_cast<const __nv_bfloat16*>(pk + PL.down_t);
   a.H = H; a.E = E; a.G = G;
   a.tau_b = __bfloat162float(__float2bfloat16_rn(tau));
   a.bias = bias;
@@ -535,12 +542,15 @@ int decode1_launch(const void* x, const void* packed, int H, int E, int G, float
   a.logits_out = static_cast<__nv_bfloat16*>(logits_out);
   a.weights_out = static_cast<__nv_bfloat16*>(weights_out);
   a.counts = reinterpret_cast<long long*>(counts);
-  a.part = static_cast<unsigned long long*>(part);
+  a.a2x = static_cast<unsigned long long*>(region);
+  a.presence = a.a2x + (size_t)E * G;
   a.epoch = epoch;
   a.status = status;
-  a.slots = C.slots;
-  a.pdl = pdl;
+  a.CE = C.CE;
+  a.S = C.S;
+  a.NC = C.NC;
   a.trig_early = mode == 2;
+  a.pdl = pdl;
   a.trace = trace;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];

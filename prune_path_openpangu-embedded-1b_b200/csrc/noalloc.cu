@@ -15,12 +15,12 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
 
 // Scratch limit: tokens * hidden <= 8192 (e.g. 5 tokens at hidden 1536, 4 at 2048, 16 at
 // 512) for up to 32 clusters of the multi-token decode grid (32 * 8192 * 4 bytes of
-// partials), plus the single-token kernel's tagged partials for hidden <= 1536 (160 CTAs x
-// 1536 x 8 bytes; at larger hidden sizes one token takes the multi-token kernel), plus a
-// 256-byte header.  Every GPU that loads the library holds these ~2.9 MiB until exit.
+// partials), plus the single-token kernel's exchange region for experts * group <= 16384
+// ((16384 + 160) x 8 bytes), plus a 256-byte header.  Every GPU that loads the library
+// holds these ~1.2 MiB until exit.
 constexpr int kNoAllocMaxTokHidden = 8192;
 constexpr size_t kNoAllocHeader = 256;
-constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4 + (size_t)160 * 1536 * 8;
+constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4 + (size_t)(16384 + 160) * 8;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 

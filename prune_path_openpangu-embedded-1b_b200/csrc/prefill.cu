@@ -728,6 +728,7 @@ static int make_map_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt,
 }
 
 size_t prefill_workspace_bytes(long long N, int H, int E, int G) { return prefill_ws_layout(N, H, E, G).total; }
+size_t route_workspace_bytes(long long N, int E);
 
 // mode: kPrefillFull (router -> selection -> experts -> bf16 out), kPrefillRouteOnly (stop
 // after the gate weights), kPrefillExperts (gate weights given in weights_out; expert compute
@@ -738,8 +739,11 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
                    void* out, void* logits_out, void* weights_out, int64_t* counts, void* wsp, size_t ws_bytes,
                    cudaStream_t st, int mode) {
   const PrefillWs W = prefill_ws_layout(N, H, E, G);
-  if (ws_bytes < W.total) {
-    set_error("ppmoe_prefill: workspace %zu < %zu bytes needed for %d tokens", ws_bytes, W.total, N);
+  // routing alone touches only the status word and the logits (the first two regions of the
+  // layout, identical to the routing workspace of ppmoe_route)
+  const size_t need = mode == kPrefillRouteOnly ? route_workspace_bytes(N, E) : W.total;
+  if (ws_bytes < need) {
+    set_error("ppmoe_prefill: workspace %zu < %zu bytes needed for %d tokens", ws_bytes, need, N);
     return PPMOE_ERR_WORKSPACE;
   }
   uint8_t* ws = static_cast<uint8_t*>(wsp);
@@ -766,6 +770,15 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)E}, s[1] = {(cuuint64_t)H * 2};
     cuuint32_t b[2] = {kBK, (cuuint32_t)EP};
     if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
+  }
+  if (mode == kPrefillRouteOnly) {  // router GEMM + selection only: the router rows alone are read
+    const int rstages = EP <= 128 ? 6 : 4;
+    RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+    const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
+    PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
+    router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
+    PPMOE_CHECK_CUDA(cudaGetLastError());
+    return route_logits_launch(logits, N, E, tau, nullptr, weights, nullptr, st);
   }
   {
     cuuint64_t d[3] = {(cuuint64_t)H, 2, (cuuint64_t)E * G}, s[2] = {(cuuint64_t)H * 2, (cuuint64_t)H * 6};

@@ -131,12 +131,18 @@ class ExpertParallelMoE:
         neurons = (own[:, None] * G + torch.arange(G)[None]).reshape(-1).to(W_gate.device if W_gate is not None else "cpu")
         self.route_fn = route_fn
         self.expert_fn = expert_fn
-        self.full = self.local = None
+        self.local = None
+        self.router_rows = None
+        self.logit_bias = logit_bias
+        self._route_ws = None
         if route_fn is None or expert_fn is None:
             dev = W_gate.device
-            self.full = TauSparseMoE(H, E * G, E, G, tau).to(dev)
-            self.full.W_gate, self.full.W_up, self.full.W_down, self.full.router = W_gate, W_up, W_down, router
-            self.full.logit_bias = logit_bias
+            # routing reads only the router section of a packed blob (router_eh [E][H]): keep
+            # just those rows, not a second copy of every expert's weights
+            buf = torch.empty(E * H * 2 + 1024, dtype=torch.uint8, device=dev)
+            off = (-buf.data_ptr()) % 1024
+            self.router_rows = buf[off:off + E * H * 2]
+            self.router_rows.view(torch.bfloat16).view(E, H).copy_(router.t())
             self.local = TauSparseMoE(H, self.el * G, self.el, G, tau).to(dev)
             self.local.W_gate = W_gate[:, neurons].contiguous()
             self.local.W_up = W_up[:, neurons].contiguous()
@@ -154,14 +160,17 @@ class ExpertParallelMoE:
     def _route(self, x):
         if self.route_fn is not None:
             return self.route_fn(x)
-        m = self.full
         n = x.shape[0]
         w = torch.empty(n, self.E, dtype=torch.bfloat16, device=x.device)
-        ws = m.prefill_workspace(n)
-        bias = m.logit_bias
+        nbytes = _lib.load().ppmoe_route_workspace_bytes(n, self.H, self.E, self.G)
+        if self._route_ws is None or self._route_ws.numel() < nbytes:
+            buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=x.device)
+            self._route_ws = buf[(-buf.data_ptr()) % 1024:][:nbytes]
+        ws = self._route_ws
+        bias = self.logit_bias
         if bias is not None:
             bias = bias.to(device=x.device, dtype=torch.float32).contiguous()
-        _lib.call("ppmoe_prefill_route", x.data_ptr(), n, m.packed().data_ptr(), self.H, self.E, self.G,
+        _lib.call("ppmoe_prefill_route", x.data_ptr(), n, self.router_rows.data_ptr(), self.H, self.E, self.G,
                   float(self.tau), _lib.ptr(bias), None, w.data_ptr(), ws.data_ptr(), ws.numel(),
                   _stream_handle(x.device))
         return w

@@ -50,7 +50,7 @@ def _worker(rank, world, port, q, mode):
         m = ep.ExpertParallelMoE.__new__(ep.ExpertParallelMoE)
         m.group, m.world, m.rank = None, world, rank
         m.H, m.E, m.G, m.tau, m.el = 128, 16, 32, 0.7, 16 // world
-        m.route_fn, m.expert_fn, m.full, m.local, m.last_stats = _cpu_route(L, 0.7), _cpu_experts(L), None, None, {}
+        m.route_fn, m.expert_fn, m.local, m.last_stats = _cpu_route(L, 0.7), _cpu_experts(L), None, {}
         if mode == "fail" and rank == 1:
             raise RuntimeError("injected failure before dispatch")
         y = m(shard)

@@ -70,7 +70,7 @@ def test_route_compact_bias_and_large_e(cuda):
     """Zipf prior and E = 192 / 256 (warp bitonic selection) through the same entry point."""
     synth = pkg().synth
     for (H, E, G, N, tau, bias) in [(1536, 64, 96, 300, 0.7, True), (1536, 192, 32, 50, 0.7, False),
-                                   (1536, 256, 24, 33, 0.95, False)]:
+                                   (1536, 256, 32, 33, 0.95, False)]:
         L = make_layer(12, H, E, G, tau)
         m = make_module(L, tau, cuda)
         b = synth.zipf_bias(E, 1.2) if bias else None
