@@ -192,6 +192,30 @@ PPMOE_API int ppmoe_ep_combine(const float* back, const int32_t* row_of, int ran
 PPMOE_API int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int ranks, int tokens, int hidden,
                                     void* out, void* stream);
 
+/* Expert-parallel prefill, dispatch side (no reference counterpart: the reference runs on one
+ * device; this replaces the host-side send-list construction around the NCCL all-to-all).
+ * Destination rank d owns experts d, d + ranks, d + 2 ranks, ...; a token is sent to d when it
+ * selected at least one of them (weights [tokens][experts] bf16, 0 = not selected).  The tokens
+ * go in `chunks` consecutive chunks of whole 256-token blocks (chunk c: blocks
+ * [nb c / chunks, nb (c + 1) / chunks), nb = ceil(tokens / 256)).  `send` receives one payload
+ * row of row_pitch bytes per (token, destination): hidden bf16 activations, then the token's
+ * gate weights for the destination's experts in owned order; rows chunk-major, then
+ * destination-major, tokens ascending.  counts [ranks][chunks] int64 = rows per segment;
+ * row_of [ranks][tokens] int32 = the send row of (token, destination) or -1.  Device-side only
+ * (no host synchronisation); send must hold tokens * ranks rows in the worst case.
+ * row_pitch >= 2 (hidden + experts / ranks), a multiple of 16; ranks <= 8, chunks <= 8. */
+PPMOE_API size_t ppmoe_ep_dispatch_workspace_bytes(int tokens, int ranks);
+PPMOE_API int ppmoe_ep_dispatch(const void* x, const void* weights, int tokens, int hidden, int experts, int ranks,
+                                int chunks, void* send, int row_pitch, int64_t* counts, int32_t* row_of, void* ws,
+                                size_t ws_bytes, void* stream);
+/* Expert-parallel prefill, expert side: ppmoe_prefill_experts over received payload rows
+ * (ppmoe_ep_dispatch layout: activations, then the gate weights of this rank's `experts` local
+ * experts) without unpacking them; out_f32 [rows][hidden] fp32 partial sums.  Workspace as
+ * ppmoe_prefill_workspace_bytes(rows, ...).  Replaces moe_local/global_scan, moe_dispatch and
+ * moe_fused_expert_kernel (tl:133-328, 566-604) on the expert-owning rank. */
+PPMOE_API int ppmoe_ep_experts(const void* payload, int rows, int row_pitch, const void* packed, int hidden,
+                               int experts, int group, float* out_f32, void* ws, size_t ws_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts

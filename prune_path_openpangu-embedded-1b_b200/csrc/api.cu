@@ -35,7 +35,7 @@ int route_launch(const void*, int, const void*, int, int, int, float, const floa
                  uint8_t*, void*, size_t, cudaStream_t);
 size_t prefill_workspace_bytes(long long, int, int, int);
 int prefill_launch(const void*, int, const void*, int, int, int, float, const float*, void*, void*, void*, int64_t*,
-                   void*, size_t, cudaStream_t, int);
+                   void*, size_t, cudaStream_t, int, int xpitch = 0, int wpitch = 0);
 
 // Workspace header: status word, decode arrival counters; then the decode cluster partials.
 constexpr size_t kWsHeader = 256;
@@ -331,6 +331,22 @@ int ppmoe_prefill_experts(const void* x, int tokens, const void* packed, int hid
   }
   return prefill_launch(x, tokens, packed, hidden, experts, group, 0.f, nullptr, out_f32, nullptr,
                         const_cast<void*>(weights), counts, ws, ws_bytes, static_cast<cudaStream_t>(stream), 2);
+}
+
+int ppmoe_ep_experts(const void* payload, int rows, int row_pitch, const void* packed, int hidden, int experts,
+                     int group, float* out_f32, void* ws, size_t ws_bytes, void* stream) {
+  g_err[0] = 0;
+  if (int rc = prefill_checks("ppmoe_ep_experts", payload, rows, packed, hidden, experts, group, out_f32, ws))
+    return rc;
+  const int need = (int)align_up((size_t)(hidden + experts) * 2, 16);
+  if (row_pitch < need || row_pitch % 16 != 0) {
+    set_error("ppmoe_ep_experts: row_pitch=%d must be a multiple of 16 and >= %d", row_pitch, need);
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  const uint8_t* p = static_cast<const uint8_t*>(payload);
+  return prefill_launch(p, rows, packed, hidden, experts, group, 0.f, nullptr, out_f32, nullptr,
+                        const_cast<uint8_t*>(p + (size_t)hidden * 2), nullptr, ws, ws_bytes,
+                        static_cast<cudaStream_t>(stream), 2, row_pitch / 2, row_pitch / 2);
 }
 
 size_t ppmoe_route_workspace_bytes(int tokens, int hidden, int experts, int group) {

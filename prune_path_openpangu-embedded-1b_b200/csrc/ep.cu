@@ -39,9 +39,150 @@ __global__ void ep_combine_kernel(const T* __restrict__ back, const int* __restr
   }
 }
 
+
+// ------------------------------------------------------------------ dispatch
+// Destination d owns experts d, d + P, d + 2P, ...  A token goes to d when it selected at least
+// one of them (gate weight > 0).  The send buffer is chunk-major, then destination-major, tokens
+// ascending inside each (chunk, destination) segment; each payload row is the token's H bf16
+// activations followed by its gate weights for d's experts (owned order), padded to row_pitch
+// bytes.  Chunk c covers token blocks [nb c / C, nb (c + 1) / C) of 256 tokens.
+constexpr int kEpBlock = 256;
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpMaxChunks = 8;
+
+__device__ __forceinline__ uint32_t ep_dest_bits(const __nv_bfloat16* w, int E, int P) {
+  uint32_t bits = 0;
+  for (int e = 0; e < E; ++e)
+    if (__bfloat162float(w[e]) > 0.f) bits |= 1u << (e % P);
+  return bits;
+}
+
+__global__ void ep_count_kernel(const __nv_bfloat16* __restrict__ w, int n, int E, int P, int* __restrict__ blkcnt) {
+  const int t = blockIdx.x * kEpBlock + threadIdx.x;
+  const uint32_t bits = t < n ? ep_dest_bits(w + (size_t)t * E, E, P) : 0u;
+  for (int d = 0; d < P; ++d) {
+    const int c = __syncthreads_count((bits >> d) & 1u);
+    if (threadIdx.x == 0) blkcnt[blockIdx.x * P + d] = c;
+  }
+}
+
+// One thread per (chunk, destination): segment totals, then the first send row of every block.
+__global__ void ep_scan_kernel(const int* __restrict__ blkcnt, int nb, int P, int C, int* __restrict__ blkoff,
+                               long long* __restrict__ counts) {
+  __shared__ int tot[kEpMaxChunks][kEpMaxRanks];
+  const int c = threadIdx.x / kEpMaxRanks, d = threadIdx.x % kEpMaxRanks;
+  const bool on = c < C && d < P;
+  const int b0 = on ? (int)((long long)nb * c / C) : 0, b1 = on ? (int)((long long)nb * (c + 1) / C) : 0;
+  int s = 0;
+  for (int b = b0; b < b1; ++b) s += blkcnt[b * P + d];
+  tot[c][d] = on ? s : 0;
+  __syncthreads();
+  if (!on) return;
+  int run = 0;
+  for (int cc = 0; cc < c; ++cc)
+    for (int dd = 0; dd < P; ++dd) run += tot[cc][dd];
+  for (int dd = 0; dd < d; ++dd) run += tot[c][dd];
+  counts[d * C + c] = s;
+  for (int b = b0; b < b1; ++b) {
+    blkoff[b * P + d] = run;
+    run += blkcnt[b * P + d];
+  }
+}
+
+// Per 256-token block: each selected (token, destination) gets its send row (running ballot
+// prefix in token order), row_of[d][t] records it (-1 otherwise), and one warp per token copies
+// the activation row and the destination's gate weights into the payload.
+__global__ void ep_scatter_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, int n,
+                                  int H, int E, int P, const int* __restrict__ blkoff, uint8_t* __restrict__ send,
+                                  int pitch, int* __restrict__ row_of) {
+  __shared__ int wcnt[kEpMaxRanks][kEpBlock / 32];
+  __shared__ int pos_s[kEpBlock][kEpMaxRanks];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t = blockIdx.x * kEpBlock + tid;
+  const uint32_t bits = t < n ? ep_dest_bits(w + (size_t)t * E, E, P) : 0u;
+  uint32_t bal[kEpMaxRanks];
+#pragma unroll
+  for (int d = 0; d < kEpMaxRanks; ++d) {
+    bal[d] = __ballot_sync(0xffffffffu, d < P && ((bits >> d) & 1u));
+    if (lane == 0) wcnt[d][warp] = __popc(bal[d]);
+  }
+  __syncthreads();
+  for (int d = 0; d < P; ++d) {
+    int pos = -1;
+    if ((bits >> d) & 1u) {
+      pos = blkoff[blockIdx.x * P + d] + __popc(bal[d] & ((1u << lane) - 1u));
+      for (int q = 0; q < warp; ++q) pos += wcnt[d][q];
+    }
+    pos_s[tid][d] = pos;
+    if (t < n) row_of[(size_t)d * n + t] = pos;
+  }
+  __syncthreads();
+  const int el = E / P, H8 = H / 8;
+  for (int i = warp; i < kEpBlock; i += kEpBlock / 32) {
+    const int tt = blockIdx.x * kEpBlock + i;
+    if (tt >= n) break;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)tt * H);
+    for (int d = 0; d < P; ++d) {
+      const int pos = pos_s[i][d];
+      if (pos < 0) continue;
+      uint8_t* row = send + (size_t)pos * pitch;
+      for (int c = lane; c < H8; c += 32) reinterpret_cast<uint4*>(row)[c] = xr[c];
+      for (int j = lane; j < el; j += 32)
+        reinterpret_cast<__nv_bfloat16*>(row + (size_t)H * 2)[j] = w[(size_t)tt * E + d + P * j];
+    }
+  }
+}
+
 }  // namespace ppmoe
 
 using namespace ppmoe;
+
+extern "C" size_t ppmoe_ep_dispatch_workspace_bytes(int tokens, int ranks) {
+  if (tokens < 0 || ranks < 1 || ranks > kEpMaxRanks) return 0;
+  const size_t nb = (size_t)(tokens + kEpBlock - 1) / kEpBlock;
+  return 2 * align_up(nb * ranks * 4, 256) + 256;
+}
+
+extern "C" int ppmoe_ep_dispatch(const void* x, const void* weights, int tokens, int hidden, int experts, int ranks,
+                                 int chunks, void* send, int row_pitch, int64_t* counts, int32_t* row_of, void* ws,
+                                 size_t ws_bytes, void* stream) {
+  clear_error();
+  if (ranks < 1 || ranks > kEpMaxRanks || chunks < 1 || chunks > kEpMaxChunks || tokens < 0 || hidden <= 0 ||
+      hidden % 8 != 0 || experts < ranks || experts % ranks != 0 || experts > 256) {
+    set_error("ppmoe_ep_dispatch: ranks=%d (1..%d), chunks=%d (1..%d), tokens=%d, hidden=%d (multiple of 8), "
+              "experts=%d (a multiple of ranks)", ranks, kEpMaxRanks, chunks, kEpMaxChunks, tokens, hidden, experts);
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  const int need = (int)align_up((size_t)(hidden + experts / ranks) * 2, 16);
+  if (row_pitch < need || row_pitch % 16 != 0) {
+    set_error("ppmoe_ep_dispatch: row_pitch=%d must be a multiple of 16 and >= %d", row_pitch, need);
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  if (ws_bytes < ppmoe_ep_dispatch_workspace_bytes(tokens, ranks)) {
+    set_error("ppmoe_ep_dispatch: workspace %zu < %zu bytes", ws_bytes, ppmoe_ep_dispatch_workspace_bytes(tokens, ranks));
+    return PPMOE_ERR_WORKSPACE;
+  }
+  if (!x || !weights || !send || !counts || !row_of || !ws || (reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(send)) % 16) {
+    set_error("ppmoe_ep_dispatch: null pointer, or x / send not 16-byte aligned");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nb = (tokens + kEpBlock - 1) / kEpBlock;
+  int* blkcnt = static_cast<int*>(ws);
+  int* blkoff = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + align_up((size_t)nb * ranks * 4, 256));
+  if (nb > 0) {
+    ep_count_kernel<<<nb, kEpBlock, 0, st>>>(static_cast<const __nv_bfloat16*>(weights), tokens, experts, ranks, blkcnt);
+  }
+  ep_scan_kernel<<<1, kEpMaxChunks * kEpMaxRanks, 0, st>>>(blkcnt, nb, ranks, chunks, blkoff,
+                                                           reinterpret_cast<long long*>(counts));
+  if (nb > 0) {
+    ep_scatter_kernel<<<nb, kEpBlock, 0, st>>>(static_cast<const __nv_bfloat16*>(x),
+                                               static_cast<const __nv_bfloat16*>(weights), tokens, hidden, experts,
+                                               ranks, blkoff, static_cast<uint8_t*>(send), row_pitch, row_of);
+  }
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return PPMOE_OK;
+}
 
 static int ep_combine(const void* back, bool bf16, const int32_t* row_of, int ranks, int tokens, int hidden,
                       void* out, void* stream) {

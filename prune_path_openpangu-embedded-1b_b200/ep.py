@@ -9,11 +9,12 @@ large token counts:
   routing) over all ranks instead of piling them on rank 0;
 * every rank routes its own tokens (``ppmoe_prefill_route``: tcgen05 router GEMM + selection);
 * a token row is sent once to each rank that owns at least one of its selected experts,
-  together with its gate weights for that rank's experts: a count exchange
-  (``all_to_all_single`` of int64 counts) then the payload ``all_to_all_single`` (bf16 rows,
-  bf16 gate weights);
-* each rank runs its local experts on the received rows (``ppmoe_prefill_experts``: grouped
-  tcgen05 GEMMs) and returns fp32 partial sums with a second ``all_to_all_single`` (or bf16
+  together with its gate weights for that rank's experts, as one payload row: the send rows
+  are built on the device (``ppmoe_ep_dispatch``: per-block counts, a scan, a scatter copy),
+  then a count exchange (``all_to_all_single`` of int64 counts, the one host synchronisation)
+  and one payload ``all_to_all_single`` per chunk;
+* each rank runs its local experts on the received payload rows as they are
+  (``ppmoe_ep_experts``: grouped tcgen05 GEMMs) and returns fp32 partial sums with a second ``all_to_all_single`` (or bf16
   partials in the optional reduced-traffic mode, ``partials="bf16"``);
 * the source adds the partials in rank order (deterministic) and rounds to bf16 once;
 * the tokens go through in chunks so that the all-to-all transfers of one chunk overlap the
@@ -32,7 +33,7 @@ import torch.distributed as dist
 from . import _lib
 from .tau_moe import TauSparseMoE, _stream_handle
 
-__all__ = ["ExpertParallelMoE", "dispatch_plan", "combine_partials"]
+__all__ = ["ExpertParallelMoE", "dispatch_reference", "combine_partials", "chunk_bounds", "row_pitch"]
 
 
 def owned_experts(E: int, world: int, rank: int) -> torch.Tensor:
@@ -40,71 +41,68 @@ def owned_experts(E: int, world: int, rank: int) -> torch.Tensor:
     return torch.arange(rank, E, world)
 
 
-def plan_counts(weights: torch.Tensor, world: int):
-    """Device-side half of the dispatch plan: ``sel [n, P]`` (token goes to destination) and
-    ``counts [P]`` int64 from gate weights ``[n, E]`` (0 = not selected).  No host sync."""
+def chunk_bounds(n: int, chunks: int) -> list:
+    """Token bounds of the dispatch chunks: whole 256-token blocks, chunk c = blocks
+    [nb c / C, nb (c + 1) / C) (the split ``ppmoe_ep_dispatch`` uses)."""
+    nb = (n + 255) // 256
+    return [min(n, 256 * ((nb * c) // chunks)) for c in range(chunks + 1)]
+
+
+def row_pitch(H: int, el: int) -> int:
+    """Bytes per payload row: H bf16 activations + el bf16 gate weights, 16-byte multiple."""
+    return ((H + el) * 2 + 15) // 16 * 16
+
+
+def dispatch_reference(x: torch.Tensor, weights: torch.Tensor, world: int, chunks: int, pitch: int):
+    """Torch restatement of ``ppmoe_ep_dispatch`` (CPU ranks, and the checker of the GPU
+    kernel): returns ``(send [rows, pitch] uint8, counts [P, C] int64, row_of [P, n] int32)``.
+    Rows chunk-major, destination-major, tokens ascending; a row is the token's activations then
+    its gate weights for the destination's experts (``owned_experts`` order); pad bytes 0."""
     n, E = weights.shape
+    H = x.shape[1]
     if E % world:
         raise ValueError(f"experts={E} not divisible by world size {world}")
-    wv = weights.view(n, E // world, world).transpose(1, 2)  # [n, P, E/P]: expert d + P*j at [:, d, j]
-    sel = (wv > 0).any(-1)
-    return sel, sel.sum(0).to(torch.int64)
-
-
-def plan_lists(weights: torch.Tensor, sel: torch.Tensor, counts_host, world: int):
-    """Send lists for the counts already known on the host (no further host sync): rows
-    grouped by destination rank in rank order, tokens ascending within a destination.
-    Returns ``(send_tok [total] int64, send_w [total, E/P], row_of [P, n] int32)``; ``send_w``
-    holds each row's gate weights for the destination's own experts, in ``owned_experts``
-    order; ``row_of[d, t]`` is the row of (token t, destination d), -1 if t is not sent to d."""
-    n, E = weights.shape
     el = E // world
-    total = int(sum(counts_host))
-    wv = weights.view(n, el, world).transpose(1, 2)
-    nz = torch.nonzero_static(sel.t(), size=total)  # destination-major, token-minor
-    dest, send_tok = nz[:, 0], nz[:, 1]
-    send_w = wv[send_tok, dest]
-    row_of = torch.full((world, n), -1, dtype=torch.int32, device=weights.device)
-    row_of[dest, send_tok] = torch.arange(total, dtype=torch.int32, device=weights.device)
-    return send_tok, send_w.contiguous(), row_of
+    b = chunk_bounds(n, chunks)
+    wv = weights.view(n, el, world).transpose(1, 2)  # [n, P, el]: expert d + P*j at [:, d, j]
+    sel = (wv > 0).any(-1)
+    counts = torch.zeros(world, chunks, dtype=torch.int64)
+    row_of = torch.full((world, n), -1, dtype=torch.int32)
+    segs, pos = [], 0
+    for c in range(chunks):
+        for d in range(world):
+            toks = torch.nonzero(sel[b[c]:b[c + 1], d]).flatten() + b[c]
+            counts[d, c] = len(toks)
+            row_of[d, toks] = torch.arange(pos, pos + len(toks), dtype=torch.int32)
+            segs.append((toks, d))
+            pos += len(toks)
+    send = torch.zeros(pos, pitch, dtype=torch.uint8)
+    r = 0
+    for toks, d in segs:
+        k = len(toks)
+        if k:
+            send[r:r + k, :2 * H] = x[toks].contiguous().view(torch.uint8)
+            send[r:r + k, 2 * H:2 * (H + el)] = wv[toks, d].contiguous().view(torch.uint8)
+        r += k
+    return send, counts, row_of
 
 
-def dispatch_plan(weights: torch.Tensor, world: int):
-    """Per-destination send lists from gate weights ``[n, E]`` (0 = not selected).
-
-    Returns ``(send_tok [n_send] int64, send_w [n_send, E/P], send_counts [P] int64)`` as
-    :func:`plan_lists` orders them (one host read of the counts)."""
-    sel, counts = plan_counts(weights, world)
-    tok, sw, _ = plan_lists(weights, sel, counts.tolist(), world)
-    return tok, sw, counts
-
-
-def combine_partials(back: torch.Tensor, send_tok: torch.Tensor, send_counts, n: int,
-                     row_of: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Sum fp32 partial rows into their tokens in rank order and round once to bf16.
-
-    On CUDA this is ``ppmoe_ep_combine`` over the ``[P, n]`` row table (from
-    :func:`plan_lists`, or built here); elsewhere (CPU ranks in tests)
-    destination-by-destination scatters with the same order."""
+def combine_partials(back: torch.Tensor, row_of: torch.Tensor, n: int) -> torch.Tensor:
+    """Sum the partial rows of every token in rank order (fp32 additions) and round once to
+    bf16: ``out[t] = bf16(sum_d back[row_of[d, t]])`` over the rows that exist (``ppmoe_ep_combine``
+    on CUDA; the same order with torch operations on CPU ranks)."""
+    P = row_of.shape[0]
     if back.is_cuda:
-        P = len(send_counts)
-        if row_of is None:
-            dest = torch.repeat_interleave(torch.arange(P, device=back.device),
-                                           torch.as_tensor(send_counts, device=back.device))
-            row_of = torch.full((P, n), -1, dtype=torch.int32, device=back.device)
-            row_of[dest, send_tok] = torch.arange(back.shape[0], dtype=torch.int32, device=back.device)
         out = torch.empty(n, back.shape[1], dtype=torch.bfloat16, device=back.device)
         fn = "ppmoe_ep_combine_bf16" if back.dtype == torch.bfloat16 else "ppmoe_ep_combine"
         _lib.call(fn, back.data_ptr(), row_of.data_ptr(), P, n, back.shape[1], out.data_ptr(),
                   torch.cuda.current_stream(back.device).cuda_stream)
         return out
-    acc = torch.zeros(n, back.shape[1], dtype=torch.float32, device=back.device)
-    off = 0
-    for c in send_counts:
-        c = int(c)
-        if c:
-            acc.index_add_(0, send_tok[off:off + c], back[off:off + c].float())
-        off += c
+    acc = torch.zeros(n, back.shape[1], dtype=torch.float32)
+    for d in range(P):
+        rows = row_of[d].long()
+        has = rows >= 0
+        acc[has] += back[rows[has]].float()
     return acc.to(torch.bfloat16)
 
 
@@ -175,18 +173,41 @@ class ExpertParallelMoE:
                   _stream_handle(x.device))
         return w
 
-    def _experts(self, xr, wr):
+    def _experts(self, payload):
+        """Partial sums [rows, H] fp32 of this rank's experts over received payload rows."""
+        n = payload.shape[0]
         if self.expert_fn is not None:
-            return self.expert_fn(xr, wr, owned_experts(self.E, self.world, self.rank))
-        n = xr.shape[0]
-        out = torch.empty(n, self.H, dtype=torch.float32, device=xr.device)
+            v = payload.view(torch.bfloat16)
+            return self.expert_fn(v[:, :self.H], v[:, self.H:self.H + self.el],
+                                  owned_experts(self.E, self.world, self.rank))
+        out = torch.empty(n, self.H, dtype=torch.float32, device=payload.device)
         if n == 0:
             return out
         m = self.local
         ws = m.prefill_workspace(n)
-        _lib.call("ppmoe_prefill_experts", xr.data_ptr(), n, m.packed().data_ptr(), self.H, self.el, self.G,
-                  wr.data_ptr(), out.data_ptr(), None, ws.data_ptr(), ws.numel(), _stream_handle(xr.device))
+        _lib.call("ppmoe_ep_experts", payload.data_ptr(), n, payload.shape[1], m.packed().data_ptr(), self.H,
+                  self.el, self.G, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle(payload.device))
         return out
+
+    def _dispatch(self, x, w, C, pitch):
+        if not x.is_cuda:
+            return dispatch_reference(x, w, self.world, C, pitch)
+        n, P = x.shape[0], self.world
+        dev = x.device
+        cache = getattr(self, "_dispatch_bufs", None)
+        key = (n, P, C, pitch, dev)
+        if cache is None or cache[0] != key:
+            lib = _lib.load()
+            nbytes = lib.ppmoe_ep_dispatch_workspace_bytes(n, P)
+            cache = (key, torch.empty(max(1, n * P), pitch, dtype=torch.uint8, device=dev),
+                     torch.empty(P, C, dtype=torch.int64, device=dev),
+                     torch.empty(P, n, dtype=torch.int32, device=dev),
+                     torch.empty(nbytes, dtype=torch.uint8, device=dev))
+            self._dispatch_bufs = cache
+        _, send, counts, row_of, ws = cache
+        _lib.call("ppmoe_ep_dispatch", x.data_ptr(), w.data_ptr(), n, self.H, self.E, P, C, send.data_ptr(), pitch,
+                  counts.data_ptr(), row_of.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle(dev))
+        return send, counts, row_of
 
     # ------------------------------------------------------------------ forward
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
@@ -209,57 +230,54 @@ class ExpertParallelMoE:
         x = x.to(torch.bfloat16).contiguous()
         n = x.shape[0]
         P = self.world
-        C = max(1, min(getattr(self, "chunks", 2 if P > 1 else 1), n))
-        bounds = [(n * c) // C for c in range(C + 1)]
+        C = max(1, min(getattr(self, "chunks", 2 if P > 1 else 1), (n + 255) // 256, 8))
+        pitch = row_pitch(self.H, self.el)
         mark()
         w = self._route(x)
-        cnts = [plan_counts(w[bounds[c]:bounds[c + 1]], P) for c in range(C)]
-        send_counts = torch.stack([k for _, k in cnts], 1).contiguous()  # [P dest, C]
+        send, counts, row_of = self._dispatch(x, w, C, pitch)   # device-side send rows, no sync
         if P == 1:
-            sc = send_counts.t().tolist()  # the one host synchronisation
+            sc = counts.t().tolist()                               # the one host synchronisation
             rc = sc
         else:
-            recv_counts = torch.empty_like(send_counts)                   # [P src, C]
-            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-            both = torch.stack([send_counts, recv_counts]).cpu()         # the one host synchronisation
-            sc, rc = both[0].t().tolist(), both[1].t().tolist()           # [C][P]
-        plans = [plan_lists(w[bounds[c]:bounds[c + 1]], cnts[c][0], sc[c], P) for c in range(C)]
+            recv_counts = torch.empty_like(counts)                  # [P src, C]
+            dist.all_to_all_single(recv_counts, counts, group=self.group)
+            both = torch.stack([counts, recv_counts]).cpu()        # the one host synchronisation
+            sc, rc = both[0].t().tolist(), both[1].t().tolist()     # [C][P]
+        sbase = [0]
+        for c in range(C):
+            sbase.append(sbase[-1] + sum(sc[c]))
         mark()
-        # dispatch: rows and gate weights of every chunk, asynchronously
+        # dispatch: one payload all-to-all per chunk (rows and gate weights together)
         recv, works = [], []
-        for c, (tok, sw, _) in enumerate(plans):
-            sx = x[bounds[c]:bounds[c + 1]].index_select(0, tok)
+        for c in range(C):
+            sx = send[sbase[c]:sbase[c + 1]]
             if P == 1:
-                recv.append((sx, sw))
+                recv.append(sx)
                 continue
-            rx = torch.empty(sum(rc[c]), self.H, dtype=x.dtype, device=x.device)
-            rw = torch.empty(sum(rc[c]), self.el, dtype=sw.dtype, device=x.device)
-            works.append((dist.all_to_all_single(rx, sx, rc[c], sc[c], group=self.group, async_op=True),
-                          dist.all_to_all_single(rw, sw, rc[c], sc[c], group=self.group, async_op=True)))
-            recv.append((rx, rw))
+            rx = torch.empty(sum(rc[c]), pitch, dtype=torch.uint8, device=x.device)
+            works.append(dist.all_to_all_single(rx, sx, rc[c], sc[c], group=self.group, async_op=True))
+            recv.append(rx)
         mark()
-        # experts per chunk, each followed by its combine transfer
-        backs, bworks = [], []
+        # experts per chunk, each followed by its return transfer into the chunk's rows of `back`
+        bf16_parts = getattr(self, "partials", "fp32") == "bf16"
+        back = torch.empty(sbase[C], self.H, dtype=torch.bfloat16 if bf16_parts else torch.float32,
+                           device=x.device)
+        bworks = []
         for c in range(C):
             if P > 1:
-                for wk in works[c]:
-                    wk.wait()
-            part = self._experts(*recv[c])
-            if getattr(self, "partials", "fp32") == "bf16":
+                works[c].wait()
+            part = self._experts(recv[c])
+            if bf16_parts:
                 part = part.to(torch.bfloat16)
             if P == 1:
-                backs.append(part)
+                back[sbase[c]:sbase[c + 1]] = part
                 continue
-            back = torch.empty(sum(sc[c]), self.H, dtype=part.dtype, device=x.device)
-            bworks.append(dist.all_to_all_single(back, part, sc[c], rc[c], group=self.group, async_op=True))
-            backs.append(back)
+            bworks.append(dist.all_to_all_single(back[sbase[c]:sbase[c + 1]], part, sc[c], rc[c],
+                                                 group=self.group, async_op=True))
+        for wk in bworks:
+            wk.wait()
         mark()
-        y = torch.empty(n, self.H, dtype=torch.bfloat16, device=x.device)
-        for c in range(C):
-            if P > 1:
-                bworks[c].wait()
-            y[bounds[c]:bounds[c + 1]] = combine_partials(backs[c], plans[c][0], sc[c], bounds[c + 1] - bounds[c],
-                                                          row_of=plans[c][2])
+        y = combine_partials(back, row_of, n)
         mark()
         self.last_stats = {"sent_rows": sum(sum(v) for v in sc), "recv_rows": sum(sum(v) for v in rc),
                            "chunks": C}

@@ -102,19 +102,45 @@ def test_ep_rank_failure_surfaces_as_error():
     assert res[0][0] == "err"  # the surviving rank's collective fails instead of hanging
 
 
-def test_dispatch_plan_and_combine_single_process():
+def test_dispatch_reference_and_combine_single_process():
     ep = __import__(pkg().__name__ + ".ep", fromlist=["x"])
     w = torch.zeros(5, 8, dtype=torch.bfloat16)
     w[0, 1] = 0.5; w[0, 6] = 0.25; w[2, 5] = 1.0; w[3, 0] = 0.75; w[4, 7] = 0.5; w[4, 4] = 0.5
-    tok, sw, cnt = ep.dispatch_plan(w, 2)
+    x = torch.arange(5 * 8, dtype=torch.float32).view(5, 8).to(torch.bfloat16)
+    pitch = ep.row_pitch(8, 4)
+    assert pitch == 32
+    send, cnt, row_of = ep.dispatch_reference(x, w, 2, 1, pitch)
     # rank 0 owns experts 0,2,4,6; rank 1 owns 1,3,5,7
-    assert cnt.tolist() == [3, 3]
-    assert tok.tolist() == [0, 3, 4, 0, 2, 4]
+    assert cnt.tolist() == [[3], [3]]
+    assert row_of.tolist() == [[0, -1, -1, 1, 2], [3, -1, 4, -1, 5]]
+    v = send.view(torch.bfloat16)
+    assert torch.equal(v[:, :8], x[[0, 3, 4, 0, 2, 4]])
+    sw = v[:, 8:12].float()
     assert sw[0].tolist() == [0.0, 0.0, 0.0, 0.25] and sw[1].tolist() == [0.75, 0.0, 0.0, 0.0]
     assert sw[2].tolist() == [0.0, 0.0, 0.5, 0.0] and sw[3].tolist() == [0.5, 0.0, 0.0, 0.0]
     assert sw[4].tolist() == [0.0, 0.0, 1.0, 0.0] and sw[5].tolist() == [0.0, 0.0, 0.0, 0.5]
     back = torch.arange(6 * 3, dtype=torch.float32).view(6, 3)
-    out = ep.combine_partials(back, tok, cnt.tolist(), 5)
+    out = ep.combine_partials(back, row_of, 5)
     assert out[0].float().tolist() == (back[0] + back[3]).tolist()
     assert out[4].float().tolist() == (back[2] + back[5]).tolist()
     assert out[1].float().abs().sum() == 0
+
+
+def test_dispatch_reference_chunks():
+    """Chunks are whole 256-token blocks; rows chunk-major, then destination-major."""
+    ep = __import__(pkg().__name__ + ".ep", fromlist=["x"])
+    assert ep.chunk_bounds(600, 2) == [0, 256, 600] and ep.chunk_bounds(600, 3) == [0, 256, 512, 600]
+    g = torch.Generator().manual_seed(3)
+    w = (torch.rand(600, 16, generator=g) > 0.7).to(torch.bfloat16) * 0.5
+    x = torch.randn(600, 64, generator=g).to(torch.bfloat16)
+    send, cnt, row_of = ep.dispatch_reference(x, w, 4, 3, ep.row_pitch(64, 4))
+    b = ep.chunk_bounds(600, 3)
+    pos = 0
+    for c in range(3):
+        for d in range(4):
+            k = int(cnt[d, c])
+            toks = [t for t in range(b[c], b[c + 1]) if bool((w[t, d::4] > 0).any())]
+            assert len(toks) == k
+            assert row_of[d, toks].tolist() == list(range(pos, pos + k))
+            pos += k
+    assert send.shape[0] == pos

@@ -10,7 +10,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from conftest import ROOT, assert_close_out, oracle, pkg
-from gpu_helpers import make_layer, make_module
+from gpu_helpers import assert_selection_matches, make_layer, make_module
 
 pytestmark = pytest.mark.gpu
 
@@ -46,6 +46,44 @@ def test_ep_single_rank_matches_prefill(cuda):
     assert torch.equal(epm(x).cpu(), y)
     epm.partials = "bf16"
     _close_loose(epm(x).cpu(), ref, "ep(1) bf16 partials vs prefill")
+
+
+@pytest.mark.parametrize("n,world,chunks", [(3000, 1, 1), (3000, 2, 2), (3000, 4, 3), (17, 8, 1), (4096, 8, 8)])
+def test_ep_dispatch_kernel_matches_reference(cuda, n, world, chunks):
+    """ppmoe_ep_dispatch (device send rows, counts, row table) equals its torch restatement
+    byte for byte on the defined bytes of every row."""
+    from importlib import import_module
+    ep = import_module(pkg().__name__ + ".ep")
+    L = make_layer(21, 1536, 64, 96, 0.7)
+    x = pkg().synth.make_tokens(21, n, 1536)
+    w, _ = oracle().softmax_thresholding(oracle().router_logits(x, L.router_w), 0.7)
+    pitch = ep.row_pitch(1536, 64 // world)
+    send_r, cnt_r, row_r = ep.dispatch_reference(x, w, world, chunks, pitch)
+    m = ep.ExpertParallelMoE.__new__(ep.ExpertParallelMoE)
+    m.world, m.H, m.E = world, 1536, 64
+    send, cnt, row_of = m._dispatch(x.to(cuda), w.to(cuda), chunks, pitch)
+    torch.cuda.synchronize()
+    assert torch.equal(cnt.cpu(), cnt_r)
+    assert torch.equal(row_of.cpu(), row_r)
+    k = send_r.shape[0]
+    used = 2 * (1536 + 64 // world)
+    assert torch.equal(send[:k, :used].cpu(), send_r[:, :used])
+
+
+def test_ep_single_rank_against_oracle(cuda):
+    """Expert-parallel path (device dispatch, payload experts, combine) against the oracle on
+    the first 256 tokens, logits teacher-forced from the routing call."""
+    L = make_layer(14, 1536, 64, 96, 0.7)
+    epm, m = _ep_module(L, 0.7, cuda)
+    x = pkg().synth.make_tokens(14, 1024, 1536)
+    y = epm(x.to(cuda)).cpu()
+    xs = x[:256]
+    lg = torch.empty(256, 64, dtype=torch.bfloat16, device=cuda)
+    w = torch.empty(256, 64, dtype=torch.bfloat16, device=cuda)
+    m.forward_prefill(xs.to(cuda), logits_out=lg, weights_out=w)
+    ref = oracle().moe_mlp(xs, L, 0.7, logits=lg.cpu())
+    assert_selection_matches(w.cpu(), lg.cpu(), 0.7, "ep(1) selection")
+    assert_close_out(y[:256], ref.out, "ep(1) vs oracle")
 
 
 def _nccl_worker(rank, world, port, q):
