@@ -221,7 +221,7 @@ PPMOE_API int ppmoe_ep_experts(const void* payload, int rows, int row_pitch, con
  * cudaMalloc at this point (code running inside someone else's memory pool, plugin hosts
  * that only hand over inputs and outputs, latency-critical paths where an allocation would
  * synchronise the device).  No counterpart in the reference.  Same kernel and results as
- * ppmoe_decode without bias and side outputs; its scratch is a ~1.2 MiB array inside this
+ * ppmoe_decode without bias and side outputs; its scratch is a ~1 MiB array inside this
  * library's device memory, held by every GPU that loads the library until process exit.
  *   Limit: 1 <= tokens <= 16 and tokens * hidden <= 8192 (PPMOE_ERR_UNSUPPORTED beyond).
  *   The first call on a device looks up the array's device address; make that first call

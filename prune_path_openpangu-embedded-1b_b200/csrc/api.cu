@@ -29,7 +29,6 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 void decode_set_trace(void*);
-size_t decode1_region_bytes(int E, int G);
 size_t route_workspace_bytes(long long, int);
 int route_launch(const void*, int, const void*, int, int, int, float, const float*, int32_t*, void*, int32_t*,
                  uint8_t*, void*, size_t, cudaStream_t);
@@ -96,10 +95,9 @@ int ppmoe_pack(const void* W_gate, const void* W_up, const void* W_down, const v
 size_t ppmoe_workspace_bytes(int max_tokens, int hidden, int experts, int group) {
   if (check_shape("ppmoe_workspace_bytes", hidden, experts, group) || max_tokens < 0) return 0;
   const size_t nt = (size_t)(max_tokens < PPMOE_DECODE_MAX_TOKENS ? max_tokens : PPMOE_DECODE_MAX_TOKENS);
-  // cross-cluster partials of the multi-token kernel, then the exchange region of the
-  // single-token kernel
+  // cross-cluster partials of the decode kernel
   const size_t multi = (size_t)kWsMaxClusters * (nt ? nt : 1) * hidden * 4;
-  return kWsHeader + multi + decode1_region_bytes(experts, group);
+  return kWsHeader + multi;
 }
 
 int ppmoe_workspace_init(void* ws, size_t ws_bytes, void* stream) {

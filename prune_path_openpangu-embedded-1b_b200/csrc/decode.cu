@@ -948,29 +948,10 @@ static thread_local DecodeCfgCache g_dec_cache;
 static unsigned long long* g_trace = nullptr;
 void decode_set_trace(void* buf) { g_trace = static_cast<unsigned long long*>(buf); }
 
-int decode1_launch(const void* x, const void* packed, int H, int E, int G, float tau, const float* bias, void* out,
-                   void* logits_out, void* weights_out, int64_t* counts, int pdl, cudaStream_t stream,
-                   uint32_t* status, uint32_t* epoch, void* region, size_t region_bytes,
-                   unsigned long long* trace);
-size_t decode1_region_bytes(int E, int G);
-
 int decode_launch(const void* x, int tokens, const void* packed, int H, int E, int G, float tau,
                   const float* bias, void* out, void* logits_out, void* weights_out, int64_t* counts,
                   void* wsp, size_t ws_bytes, int pdl, cudaStream_t stream, uint32_t* status,
                   uint32_t* counters, float* cpart, size_t cpart_bytes, int x_host) {
-  // The single-token kernel (decode1.cu) where its shape limits allow.  Its exchange region
-  // lives at the END of the partial area (this kernel's cluster partials at its start), so the
-  // two never overlap in a workspace sized by ppmoe_workspace_bytes; its epoch word is word 8
-  // of the counter line (this kernel uses words 0-7).
-  if (tokens == 1) {
-    const size_t r1 = decode1_region_bytes(E, G);
-    if (cpart_bytes >= r1) {
-      const size_t off = (cpart_bytes - r1) & ~(size_t)255;
-      const int rc = decode1_launch(x, packed, H, E, G, tau, bias, out, logits_out, weights_out, counts, pdl, stream,
-                                    status, counters + 8, reinterpret_cast<uint8_t*>(cpart) + off, r1, g_trace);
-      if (rc != 0) return rc < 0 ? rc : PPMOE_OK;
-    }
-  }
   if (E % kCluster != 0 || H % 32 != 0) {
     set_error("ppmoe_decode: experts (%d) must be a multiple of 8 and hidden (%d) of 32", E, H);
     return PPMOE_ERR_UNSUPPORTED;

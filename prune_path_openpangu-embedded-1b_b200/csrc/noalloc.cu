@@ -14,13 +14,11 @@ int decode_launch(const void*, int, const void*, int, int, int, float, const flo
                   int64_t*, void*, size_t, int, cudaStream_t, uint32_t*, uint32_t*, float*, size_t, int x_host = 0);
 
 // Scratch limit: tokens * hidden <= 8192 (e.g. 5 tokens at hidden 1536, 4 at 2048, 16 at
-// 512) for up to 32 clusters of the multi-token decode grid (32 * 8192 * 4 bytes of
-// partials), plus the single-token kernel's exchange region for experts * group <= 16384
-// ((16384 + 160) x 8 bytes), plus a 256-byte header.  Every GPU that loads the library
-// holds these ~1.2 MiB until exit.
+// 512) for up to 32 clusters of the decode grid: 32 * 8192 * 4 bytes of partials plus a
+// 256-byte header.  Every GPU that loads the library holds this ~1 MiB until exit.
 constexpr int kNoAllocMaxTokHidden = 8192;
 constexpr size_t kNoAllocHeader = 256;
-constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4 + (size_t)(16384 + 160) * 8;
+constexpr size_t kNoAllocBytes = kNoAllocHeader + (size_t)32 * kNoAllocMaxTokHidden * 4;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
@@ -81,9 +79,8 @@ extern "C" int ppmoe_decode_noalloc(const void* x, int tokens, const void* packe
   void* ws = nullptr;
   if (int rc = scratch_address(&ws)) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // status word and arrival counters must start at zero (a previous call may have timed out);
-  // the single-token kernel's epoch word (header word 24) keeps counting
-  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 96, st));
+  // status word and arrival counters must start at zero (a previous call may have timed out)
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, kNoAllocHeader, st));
   uint8_t* w8 = static_cast<uint8_t*>(ws);
   return decode_launch(x, tokens, packed, hidden, experts, group, tau, nullptr, out, nullptr, nullptr, nullptr,
                        ws, kNoAllocBytes, 0, st, reinterpret_cast<uint32_t*>(w8),
@@ -104,7 +101,7 @@ extern "C" int ppmoe_decode_noalloc_status(void* stream) {
   PPMOE_CHECK_CUDA(cudaMemcpyAsync(&word, ws, 4, cudaMemcpyDeviceToHost, st));
   PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
   if (word == 0) return PPMOE_OK;
-  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, 96, st));
+  PPMOE_CHECK_CUDA(cudaMemsetAsync(ws, 0, kNoAllocHeader, st));
   PPMOE_CHECK_CUDA(cudaStreamSynchronize(st));
   if (word & DEVERR_TIMEOUT) {
     set_error("ppmoe_decode_noalloc: a bounded device-side wait timed out (status 0x%x)", word);

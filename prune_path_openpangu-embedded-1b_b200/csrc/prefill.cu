@@ -28,12 +28,10 @@ int route_compact_launch(const void*, int, int, float, int32_t*, void*, int32_t*
 
 constexpr int kTileM = 128;
 constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
-constexpr int kCombineTB = 32;    // tokens per combine block of the fused down + combine kernel
-constexpr int kMaxProgress = 1024;  // progress words (>= SMs)
 
 struct PrefillWs {
   size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, unit_tile, pair_token,
-      pair_w, a2, ypart, tok_pairs, tok_k, sorted_tile, sorted_key, blk_units, progress, status, total;
+      pair_w, a2, ypart, tok_pairs, tok_k, status, total;
   long long max_pairs, max_tiles;
   int nblocks;
 };
@@ -62,10 +60,6 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   w.ypart = take((size_t)w.max_pairs * H * 3);  // 24-bit down-projection row of every pair (2 planes)
   w.tok_pairs = take((size_t)N * E * 4);        // per token: its pairs in expert order
   w.tok_k = take((size_t)N * 4);
-  w.sorted_tile = take((size_t)w.max_tiles * 4);
-  w.sorted_key = take((size_t)w.max_tiles * 4);
-  w.blk_units = take((size_t)((N + kCombineTB - 1) / kCombineTB) * 4);
-  w.progress = take((size_t)kMaxProgress * 4);
   w.total = o;
   return w;
 }
@@ -679,342 +673,6 @@ __global__ void pair_combine_kernel(const uint4* __restrict__ yhi, const uint2* 
   }
 }
 
-// ======================================================================== fused down GEMM + combine
-// One persistent launch replaces down_gemm_kernel + pair_combine_kernel.  The down GEMM's work
-// units (tile, group of NCG 128-column chunks) run in the order of each tile's first token, so
-// the pair rows of the tokens at the front of that order are complete early; combine warps in
-// every CTA sum those tokens' rows (expert order, fp32, as pair_combine_kernel) while the GEMM
-// carries on with later tokens, and then discard the rows' L2 lines (discard.global.L2: no
-// write-back to HBM).  The pair rows therefore live and die in L2 instead of crossing HBM
-// twice.  Readiness: CTA b publishes how many of its units (b, b + grid, ...) have their stores
-// complete; token block j waits until every unit of the first blk_units[j] in the order is
-// complete (every tile that holds one of the block's tokens starts at or before the block's
-// last token).  The readiness polls need every CTA resident (one CTA per SM, grid = SMs); every
-// poll is bounded.
-struct DCArgs {
-  int H, G, NCW, NCG, NGRP;      // NGRP = H / NCW / NCG unit groups per tile
-  const int* tile_expert;
-  const int* tile_row0;
-  const int* ntiles;
-  const int* sorted_tile;        // tiles in order of first token (ties: lower expert first)
-  const int* blk_units;          // per token block: length of the unit prefix it needs
-  unsigned* progress;            // [grid] completed units per CTA (zeroed by tile_order_kernel)
-  const uint4* yhi;              // pair-row planes (what mapYh / mapYl store)
-  const uint2* ylo;
-  const int* tok_pairs;
-  const int* tok_k;
-  int E, N, TB, nblk, f32out, discard;
-  void* out;
-  uint32_t* status;
-};
-
-constexpr int kDCThreads = 320;     // warps 0-3 epilogue, 4 TMA, 5 MMA, 6-9 combine
-constexpr unsigned long long kDCPollNs = 2000000000ull;  // readiness poll limit (2 s)
-
-__device__ __forceinline__ unsigned long long dc_now() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// wait until at most n bulk groups of this thread are pending (n <= 8)
-__device__ __forceinline__ void bulk_wait_dyn(int n) {
-  switch (n) {
-    case 0: bulk_wait<0>(); break;
-    case 1: bulk_wait<1>(); break;
-    case 2: bulk_wait<2>(); break;
-    case 3: bulk_wait<3>(); break;
-    case 4: bulk_wait<4>(); break;
-    case 5: bulk_wait<5>(); break;
-    case 6: bulk_wait<6>(); break;
-    case 7: bulk_wait<7>(); break;
-    default: bulk_wait<8>(); break;
-  }
-}
-__device__ __forceinline__ void dc_publish(unsigned* p, unsigned v) {
-  asm volatile("fence.proxy.async.global;" ::: "memory");  // the bulk stores, before the release
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__global__ void __launch_bounds__(kDCThreads, 1)
-down_combine_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
-                    const __grid_constant__ CUtensorMap mapYh, const __grid_constant__ CUtensorMap mapYl,
-                    const DCArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int KB2 = (a.G + kBK - 1) / kBK;
-  const uint32_t a_kb = kTileM * 128, b_kb = (uint32_t)a.NCW * 128;
-  const uint32_t a_bytes = KB2 * a_kb, b_bytes = KB2 * b_kb;
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + a_bytes;
-  uint64_t* bfull = reinterpret_cast<uint64_t*>(sB + kDownStages * b_bytes);
-  uint64_t* bempty = bfull + kDownStages;
-  uint64_t* afull = bempty + kDownStages;
-  uint64_t* aempty = afull + 1;
-  uint64_t* tfull = aempty + 1;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 1024));
-  const int nunits = a.ntiles[0] * a.NGRP;
-  const int P = gridDim.x, bid = blockIdx.x;
-  if (tid == 0) {
-    for (int s = 0; s < kDownStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
-    mbar_init(afull, 1);
-    mbar_init(aempty, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
-    fence_mbar_init();
-  }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 4 && lane == 0) {  // TMA producer
-    int ul = 0, ch = 0;
-    for (int u = bid; u < nunits; u += P, ++ul) {
-      const int tile = a.sorted_tile[u / a.NGRP], c0 = (u % a.NGRP) * a.NCG;
-      const int e = a.tile_expert[tile], row0 = a.tile_row0[tile];
-      mbar_wait_parked(aempty, (ul & 1) ^ 1, a.status);
-      mbar_arrive_expect_tx(afull, a_bytes);
-      for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + kb * a_kb, &mapA2, kb * kBK, row0, afull);
-      for (int c = c0; c < c0 + a.NCG; ++c, ++ch) {
-        const int s = ch % kDownStages;
-        mbar_wait_parked(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
-        mbar_arrive_expect_tx(&bfull[s], b_bytes);
-        for (int kb = 0; kb < KB2; ++kb)
-          tma_load_2d(sB + s * b_bytes + kb * b_kb, &mapD, kb * kBK, e * a.H + c * a.NCW, &bfull[s]);
-      }
-    }
-  } else if (warp == 5 && lane == 0) {  // MMA issuer
-    const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
-    int ul = 0, ch = 0;
-    for (int u = bid; u < nunits; u += P, ++ul) {
-      mbar_wait_parked(afull, ul & 1, a.status);
-      tc_fence_after();
-      for (int c = 0; c < a.NCG; ++c, ++ch) {
-        const int s = ch % kDownStages, acc = ch & 1;
-        mbar_wait_parked(&tempty[acc], ((ch >> 1) & 1) ^ 1, a.status);
-        mbar_wait_parked(&bfull[s], (ch / kDownStages) & 1, a.status);
-        tc_fence_after();
-        for (int k16 = 0; k16 < a.G / 16; ++k16) {
-          const int kb = k16 >> 2, kk = k16 & 3;
-          const uint64_t ad = umma_desc_sw128(smem_u32(sA + kb * a_kb)) + 2 * kk;
-          const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * b_bytes + kb * b_kb)) + 2 * kk;
-          umma_bf16(tmem + acc * 256, ad, bd, idesc, k16 != 0);
-        }
-        umma_commit(&bempty[s]);
-        umma_commit(&tfull[acc]);
-      }
-      umma_commit(aempty);
-    }
-  } else if (warp < 4) {  // epilogue: 24-bit pair rows, as down_gemm_kernel
-    const int r = warp * 32 + lane;
-    const int spu = a.NCG * (a.NCW / 64);  // bulk groups committed per unit
-    int ch = 0, sub = 0, ul = 0;
-    for (int u = bid; u < nunits; u += P, ++ul) {
-      const int tile = a.sorted_tile[u / a.NGRP], cg0 = (u % a.NGRP) * a.NCG;
-      const int row0 = a.tile_row0[tile];
-      for (int c = cg0; c < cg0 + a.NCG; ++c, ++ch) {
-        const int acc = ch & 1;
-        mbar_wait_parked(&tfull[acc], (ch >> 1) & 1, a.status);
-        tc_fence_after();
-        for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
-          uint8_t* hb = stg + (sub & 1) * 24576;
-          uint8_t* lb = hb + 16384;
-          if (r == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            float v[32];
-            tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32 * half, v);
-            uint32_t w[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]) + 0x80u;  // round at bit 8
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              *reinterpret_cast<uint4*>(hb + sw128_offset(r, 4 * half + j)) =
-                  make_uint4(__byte_perm(w[8 * j], w[8 * j + 1], 0x7632), __byte_perm(w[8 * j + 2], w[8 * j + 3], 0x7632),
-                             __byte_perm(w[8 * j + 4], w[8 * j + 5], 0x7632), __byte_perm(w[8 * j + 6], w[8 * j + 7], 0x7632));
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              uint32_t w4[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int b = 16 * j + 4 * q;
-                w4[q] = __byte_perm(__byte_perm(w[b], w[b + 1], 0x0051), __byte_perm(w[b + 2], w[b + 3], 0x0051), 0x5410);
-              }
-              *reinterpret_cast<uint4*>(lb + sw64_offset(r, 2 * half + j)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
-          }
-          fence_proxy_async();
-          named_bar_sync(1, 128);
-          if (r == 0) {
-            tma_store_2d(&mapYh, hb, c * a.NCW + c0, row0);
-            tma_store_2d(&mapYl, lb, c * a.NCW + c0, row0);
-            bulk_commit();
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(&tempty[acc]);
-      }
-      // every group but this unit's is complete: units 0 .. ul - 1 of this CTA are in memory
-      if (r == 0 && ul > 0) {
-        bulk_wait_dyn(spu);
-        dc_publish(a.progress + bid, (unsigned)ul);
-      }
-    }
-    if (r == 0) {
-      bulk_wait<0>();
-      dc_publish(a.progress + bid, (unsigned)ul);
-    }
-  } else if (warp >= 6) {  // combine: token blocks bid, bid + grid, ...
-    const int cw = warp - 6;
-    const int H8 = a.H / 8;
-    int* rows_s = reinterpret_cast<int*>(stg + 2 * 24576) + cw * 256;  // this warp's token rows
-    for (int j = bid; j < a.nblk; j += P) {
-      const unsigned need = (unsigned)a.blk_units[j];
-      const unsigned long long t0 = dc_now();
-      for (uint32_t it = 0;; ++it) {
-        bool ok = true;
-        for (int b = lane; b < P; b += 32) {
-          const unsigned req = need > (unsigned)b ? (need - (unsigned)b + (unsigned)P - 1u) / (unsigned)P : 0u;
-          unsigned v;
-          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.progress + b) : "memory");
-          ok = ok && v >= req;
-        }
-        if (__all_sync(0xffffffffu, ok)) break;
-        if ((it & 63u) == 63u) {
-          if (*reinterpret_cast<volatile uint32_t*>(a.status) || dc_now() - t0 > kDCPollNs) {
-            if (lane == 0) atomicOr(a.status, DEVERR_TIMEOUT);
-            break;
-          }
-        }
-        __nanosleep(256);
-      }
-      const int tb = j * a.TB, te = min(a.N, tb + a.TB);
-      for (int t = tb + cw; t < te; t += 4) {
-        const int k = a.tok_k[t];
-        __syncwarp();
-        for (int q = lane; q < k; q += 32) rows_s[q] = a.tok_pairs[(size_t)t * a.E + q];
-        __syncwarp();
-        for (int c = lane; c < H8; c += 32) {
-          float s[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) s[i] = 0.f;
-          int q0 = 0;
-          for (; q0 + 4 <= k; q0 += 4) {
-            uint4 h[4];
-            uint2 l[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const size_t o = (size_t)rows_s[q0 + q] * H8 + c;
-              h[q] = __ldcg(a.yhi + o);
-              l[q] = __ldcg(a.ylo + o);
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float f[8];
-              unpack24(h[q].x, h[q].y, l[q].x, f);
-              unpack24(h[q].z, h[q].w, l[q].y, f + 4);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) s[i] += f[i];
-            }
-          }
-          for (; q0 < k; ++q0) {
-            const size_t o = (size_t)rows_s[q0] * H8 + c;
-            const uint4 h = __ldcg(a.yhi + o);
-            const uint2 l = __ldcg(a.ylo + o);
-            float f[8];
-            unpack24(h.x, h.y, l.x, f);
-            unpack24(h.z, h.w, l.y, f + 4);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) s[i] += f[i];
-          }
-          if (a.f32out) {
-            float4* o = static_cast<float4*>(a.out) + ((size_t)t * H8 + c) * 2;
-            o[0] = make_float4(s[0], s[1], s[2], s[3]);
-            o[1] = make_float4(s[4], s[5], s[6], s[7]);
-          } else {
-            uint32_t pk[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(s[2 * i], s[2 * i + 1]);
-              pk[i] = *reinterpret_cast<uint32_t*>(&b2);
-            }
-            static_cast<uint4*>(a.out)[(size_t)t * H8 + c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          }
-        }
-        if (a.discard) {  // the token's rows are consumed: drop their lines from L2 unwritten
-          __syncwarp();
-          const int lh = a.H / 64, ll = a.H / 128;  // 128-byte lines per high / low row
-          for (int q = 0; q < k; ++q) {
-            const int row = rows_s[q];
-            for (int li = lane; li < lh + ll; li += 32) {
-              const char* p = li < lh ? reinterpret_cast<const char*>(a.yhi + (size_t)row * H8) + 128 * li
-                                      : reinterpret_cast<const char*>(a.ylo + (size_t)row * H8) + 128 * (li - lh);
-              asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
-            }
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// Order of the down GEMM's tiles by first token (one warp per tile).  An expert's tiles are
-// consecutive and already in token order, so a tile's rank is the sum over experts of how many
-// of their tiles start before it (binary search per expert; ties go to the lower expert).
-__global__ void tile_rank_kernel(const int* __restrict__ ntiles, const int* __restrict__ tile_expert,
-                                 const int* __restrict__ pair_token, const int* __restrict__ exp_off,
-                                 const int* __restrict__ count, int E, int* __restrict__ sorted_tile,
-                                 int* __restrict__ sorted_key) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-  if (t >= ntiles[0]) return;
-  const int e = tile_expert[t], key = pair_token[(size_t)t * kTileM];
-  int cnt = 0;
-  for (int f = lane; f < E; f += 32) {
-    const int base = exp_off[f] / kTileM, nt = (count[f] + kTileM - 1) / kTileM;
-    if (f == e) { cnt += t - base; continue; }
-    int lo = 0, hi = nt;
-    while (lo < hi) {
-      const int mid = (lo + hi) >> 1;
-      const int kf = pair_token[(size_t)(base + mid) * kTileM];
-      if (f < e ? kf <= key : kf < key) lo = mid + 1; else hi = mid;
-    }
-    cnt += lo;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-  if (lane == 0) {
-    sorted_tile[cnt] = t;
-    sorted_key[cnt] = key;
-  }
-}
-
-// Per combine block of TB tokens: the number of units (tiles starting at or before the block's
-// last token, times the unit groups per tile) that must be complete.  Also clears the
-// per-CTA progress words of down_combine_kernel.
-__global__ void block_ready_kernel(const int* __restrict__ ntiles, const int* __restrict__ sorted_key, int N, int TB,
-                                   int nblk, int ngrp, int* __restrict__ blk_units, unsigned* __restrict__ progress,
-                                   int nprog) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j < nprog) progress[j] = 0u;
-  if (j >= nblk) return;
-  const int last = min(N, (j + 1) * TB) - 1;
-  int lo = 0, hi = ntiles[0];
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (sorted_key[mid] <= last) lo = mid + 1; else hi = mid;
-  }
-  blk_units[j] = lo * ngrp;
-}
-
 // ======================================================================== host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1077,16 +735,6 @@ size_t route_workspace_bytes(long long N, int E);
 // after the gate weights), kPrefillExperts (gate weights given in weights_out; expert compute
 // only; `out` receives fp32 partial sums instead of bf16).
 enum { kPrefillFull = 0, kPrefillRouteOnly = 1, kPrefillExperts = 2 };
-
-// PPMOE_PREFILL_FUSED=0 selects the two-kernel down GEMM + combine (A/B measurements).
-static int prefill_fused() {
-  static int v = -1;
-  if (v < 0) {
-    const char* s = getenv("PPMOE_PREFILL_FUSED");
-    v = s ? atoi(s) : 1;
-  }
-  return v;
-}
 
 int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G, float tau, const float* bias,
                    void* out, void* logits_out, void* weights_out, int64_t* counts, void* wsp, size_t ws_bytes,
@@ -1205,47 +853,18 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     if ((rc = make_map_2d(&mYh, y_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_128B, d, sh, b))) return rc;
     if ((rc = make_map_2d(&mYl, y_lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_64B, d, sl, b))) return rc;
   }
+  DownArgs da{H, G, NCW, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
-  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW * 128 + 256 +
-                        2 * 24576 + 1024 + 4 * 256 * 4;  // + the combine warps' row lists
+  const int NCW_ = NCW;
+  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
+                        2 * 24576 + 1024;
+  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
+  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, mYl, da);
+  PPMOE_CHECK_CUDA(cudaGetLastError());
   int* tok_pairs = reinterpret_cast<int*>(ws + W.tok_pairs);
   int* tok_k = reinterpret_cast<int*>(ws + W.tok_k);
   const uint4* yh = reinterpret_cast<const uint4*>(y_hi);
   const uint2* yl = reinterpret_cast<const uint2*>(y_lo);
-  if (prefill_fused()) {
-    // fused down GEMM + combine: units of NCG column chunks (8 bulk groups per unit)
-    const int NCH = H / NCW;
-    int NCG = std::max(1, 512 / NCW);
-    while (NCG > 1 && NCH % NCG) --NCG;
-    const int dgrid = std::min(nsm, kMaxProgress);
-    int per_sm = 0;
-    PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-    PPMOE_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, down_combine_kernel, kDCThreads, d_smem));
-    if (per_sm < 1) {
-      set_error("ppmoe_prefill: the fused down kernel does not fit on an SM");
-      return PPMOE_ERR_UNSUPPORTED;
-    }
-    int* sorted_tile = reinterpret_cast<int*>(ws + W.sorted_tile);
-    int* sorted_key = reinterpret_cast<int*>(ws + W.sorted_key);
-    int* blk_units = reinterpret_cast<int*>(ws + W.blk_units);
-    unsigned* progress = reinterpret_cast<unsigned*>(ws + W.progress);
-    const int nblk = (N + kCombineTB - 1) / kCombineTB;
-    tile_rank_kernel<<<(unsigned)((W.max_tiles + 7) / 8), 256, 0, st>>>(ntiles, tile_expert, pair_token, exp_off, count, E,
-                                                                        sorted_tile, sorted_key);
-    const int nthr = std::max(nblk, kMaxProgress);
-    block_ready_kernel<<<(nthr + 255) / 256, 256, 0, st>>>(ntiles, sorted_key, N, kCombineTB, nblk, NCH / NCG, blk_units,
-                                                           progress, kMaxProgress);
-    DCArgs dc{H, G, NCW, NCG, NCH / NCG, tile_expert, tile_row0, ntiles, sorted_tile, blk_units, progress, yh, yl,
-              tok_pairs, tok_k, E, N, kCombineTB, nblk, mode == kPrefillExperts ? 1 : 0, H % 128 == 0 ? 1 : 0, out,
-              status};
-    down_combine_kernel<<<dgrid, kDCThreads, d_smem, st>>>(mA2, mD, mYh, mYl, dc);
-    PPMOE_CHECK_CUDA(cudaGetLastError());
-    return PPMOE_OK;
-  }
-  DownArgs da{H, G, NCW, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
-  PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, mYl, da);
-  PPMOE_CHECK_CUDA(cudaGetLastError());
   const int H8 = H / 8, cthreads = std::min(256, (H8 + 31) / 32 * 32);
   if (mode == kPrefillExperts)
     pair_combine_kernel<true><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);

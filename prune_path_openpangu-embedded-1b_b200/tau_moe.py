@@ -243,15 +243,19 @@ class TauSparseMoE(nn.Module):
 
 
 class IntegratedOpenPanguMoEMLP(nn.Module):
-    """Eval-mode stand-in for the reference MLP wrapper (src/openpangu_moe.py:43-130).
+    """The reference MLP wrapper (src/openpangu_moe.py:43-130).
 
-    ``forward`` routes hidden states through ``self.tau_moe`` and unwraps a tuple as the
-    reference does (:125-130).  The training branch (dense projections + ``MoELayer``) is
-    not part of this library; calling the module in training mode raises.
-    """
+    Eval mode: ``forward`` routes hidden states through ``self.tau_moe`` (the fused CUDA path)
+    and unwraps a tuple as the reference does (:125-130).  Training mode (:98-123): the dense
+    gate/up projections of ``original_mlp``, the training router ``self.moelayer``
+    (:class:`~.training.TrainingMoELayer`: GPU selection, autograd through the gate weights
+    and softmax), the neuron mask, the down projection; the softmax probabilities are
+    appended to ``penalize_logits_list`` for the entropy and load-balance losses
+    (:func:`~.training.moe_aux_losses`)."""
 
     def __init__(self, config, train_args, original_mlp=None, penalize_logits_list=None):
         super().__init__()
+        from .training import TrainingMoELayer
         hidden = getattr(config, "hidden_size", 1536)
         inter = getattr(config, "intermediate_size", hidden * 4)
         experts = inter // train_args.group_size
@@ -259,12 +263,21 @@ class IntegratedOpenPanguMoEMLP(nn.Module):
         self.gate_proj = getattr(original_mlp, "gate_proj", None)
         self.up_proj = getattr(original_mlp, "up_proj", None)
         self.down_proj = getattr(original_mlp, "down_proj", None)
+        self.act_fn = getattr(original_mlp, "act_fn", None) or nn.SiLU()
+        self.penalize_logits_list = penalize_logits_list if penalize_logits_list is not None else []
+        self.moelayer = TrainingMoELayer(hidden, inter, experts, getattr(train_args, "tau", 0.95))
         self.tau_moe = TauSparseMoE(hidden, inter, experts, train_args.group_size,
                                     getattr(train_args, "tau", 0.5))
 
     def forward(self, hidden_states, *args, **kwargs):
         if self.training:
-            raise NotImplementedError("training-mode MoE routing is not provided by this library")
+            if self.gate_proj is None or self.up_proj is None or self.down_proj is None:
+                raise NotImplementedError("training mode needs gate_proj, up_proj and down_proj")
+            inter = self.act_fn(self.gate_proj(hidden_states)) * self.up_proj(hidden_states)
+            inter, probs = self.moelayer(hidden_states, inter)
+            if probs is not None:
+                self.penalize_logits_list.append(probs)
+            return self.down_proj(inter)
         out = self.tau_moe(hidden_states)
         return out[0] if isinstance(out, tuple) else out
 

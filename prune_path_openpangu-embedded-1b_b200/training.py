@@ -15,9 +15,12 @@ from typing import Iterable, Optional, Tuple
 
 import torch
 
+import torch.nn as nn
+import torch.nn.functional as F
+
 from . import _lib
 
-__all__ = ["route_training", "moe_aux_losses"]
+__all__ = ["route_training", "moe_aux_losses", "TrainingMoELayer"]
 
 
 def route_training(logits: torch.Tensor, tau: float) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -70,3 +73,47 @@ def moe_aux_losses(probs_list: Iterable[torch.Tensor], num_experts: int, gamma: 
         lb = lb + (avg ** 2).sum() * num_experts * lb_gamma
     n = len(probs_list)
     return ent / n, lb / n
+
+
+class TrainingMoELayer(nn.Module):
+    """Training-mode router and neuron mask of one MLP (``MoELayer``, src/MoEBlock.py:105-208).
+
+    Same parameters and buffers as the reference, so checkpoints load by key:
+    ``mlp_router.0.weight [E, H]`` (zero-initialised, ``router_weights_init``),
+    ``experts_masks [E, I]`` (neuron -> expert one-hot; contiguous groups when ``experts_id``
+    is None) and ``activated_statistics [E]``.
+
+    ``forward(hidden_states, intermediate) -> (intermediate * (y_gated @ experts_masks), y_soft)``
+    in training mode.  The selection (softmax, descending sort, cumulative mass < tau, top-1
+    guard) runs on the GPU (``ppmoe_route_logits_train``) on the detached bf16 router logits;
+    the differentiable outputs are then formed with autograd from the same logits:
+    ``y_gated = sigmoid(where(selected, logits, finfo.min))`` and ``y_soft = softmax(logits)``
+    (src/MoEBlock.py:68, 89-94), so gradients reach the router as in the reference.  In eval
+    mode it updates ``activated_statistics`` and returns ``(masked intermediate, None)``."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, experts: int, tau: float = 0.95,
+                 experts_id: Optional[torch.Tensor] = None):
+        super().__init__()
+        if intermediate_size % experts:
+            raise ValueError(f"intermediate_size={intermediate_size} not divisible by experts={experts}")
+        self.experts, self.tau = experts, tau
+        self.mlp_router = nn.Sequential(nn.Linear(hidden_size, experts, bias=False))
+        nn.init.zeros_(self.mlp_router[0].weight)
+        if experts_id is None:
+            experts_id = torch.arange(intermediate_size) // (intermediate_size // experts)
+        masks = F.one_hot(torch.as_tensor(experts_id, dtype=torch.long), num_classes=experts).t()
+        self.register_buffer("experts_masks", masks.to(self.mlp_router[0].weight.dtype))
+        self.register_buffer("activated_statistics", torch.zeros(experts, dtype=torch.long))
+
+    def forward(self, hidden_states: torch.Tensor, intermediate: torch.Tensor):
+        score = self.mlp_router(hidden_states)
+        with torch.no_grad():
+            y_sel, _ = route_training(score.detach(), self.tau)
+        selected = y_sel > 0
+        y_gated = torch.sigmoid(torch.where(selected, score, torch.full_like(score, torch.finfo(score.dtype).min)))
+        if not self.training:
+            self.activated_statistics.add_(selected.reshape(-1, self.experts).long().sum(0))
+        out = intermediate * (y_gated @ self.experts_masks.to(y_gated.dtype))
+        if not self.training:
+            return out, None
+        return out, torch.softmax(score, dim=-1)

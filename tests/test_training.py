@@ -6,7 +6,7 @@ import pytest
 import torch
 
 from conftest import oracle, pkg
-from gpu_helpers import ulp_diff_bf16
+from gpu_helpers import assert_selection_matches, ulp_diff_bf16
 
 
 def _reference_losses(probs_list, mask, E, gamma, lb_gamma):
@@ -59,3 +59,49 @@ def test_route_training_outputs(cuda, E):
     lib.call("ppmoe_route_logits", lg.to(cuda).data_ptr(), 2100, E, 0.7, w_inf.data_ptr(), None,
              torch.cuda.current_stream().cuda_stream)
     assert torch.equal(w.view(2100, E), w_inf)
+
+
+@pytest.mark.gpu
+def test_training_branch_against_reference_math(cuda):
+    """IntegratedOpenPanguMoEMLP in training mode (src/openpangu_moe.py:98-123): the selection
+    comes from the GPU kernel, y_gated / y_soft / the masked down projection and the router
+    gradient equal the reference's formulas (src/MoEBlock.py:49-95, 164-208) evaluated with
+    the oracle's selection on the same bf16 logits."""
+    import types
+    import torch.nn as nn
+    P = pkg()
+    H, I, G = 256, 512, 32
+    E = I // G
+    g = torch.Generator().manual_seed(5)
+    mlp = types.SimpleNamespace(gate_proj=nn.Linear(H, I, bias=False), up_proj=nn.Linear(H, I, bias=False),
+                                down_proj=nn.Linear(I, H, bias=False), act_fn=nn.SiLU())
+    for lin in (mlp.gate_proj, mlp.up_proj, mlp.down_proj):
+        lin.weight.data = (torch.randn(lin.weight.shape, generator=g) * 0.05)
+    cfg = types.SimpleNamespace(hidden_size=H, intermediate_size=I)
+    targs = types.SimpleNamespace(group_size=G, tau=0.7)
+    probs = []
+    m = P.IntegratedOpenPanguMoEMLP(cfg, targs, mlp, probs)
+    m.moelayer.mlp_router[0].weight.data = torch.randn(E, H, generator=g) * 0.2
+    m = m.to(device=cuda, dtype=torch.bfloat16).train()
+    x = torch.randn(2, 300, H, generator=g).to(torch.bfloat16).to(cuda)
+    y = m(x)
+    assert len(probs) == 1 and probs[0].shape == (2, 300, E)
+    y.float().square().mean().backward()
+    gr = m.moelayer.mlp_router[0].weight.grad.clone()
+
+    # the reference formulas with the oracle's selection
+    W = m.moelayer.mlp_router[0].weight.detach().clone().requires_grad_(True)
+    score = torch.nn.functional.linear(x, W)
+    w_k, _ = pkg().training.route_training(score.detach(), 0.7)
+    assert_selection_matches(w_k.cpu().reshape(-1, E), score.detach().cpu().reshape(-1, E), 0.7, "training mask")
+    sel = w_k > 0
+    y_g = torch.sigmoid(torch.where(sel, score, torch.full_like(score, torch.finfo(score.dtype).min)))
+    inter = m.act_fn(m.gate_proj(x)) * m.up_proj(x)
+    y_ref = m.down_proj(inter * (y_g @ m.moelayer.experts_masks))
+    assert torch.equal(y.detach(), y_ref.detach())
+    assert torch.equal(probs[0].detach(), torch.softmax(score.detach(), -1))
+    y_ref.float().square().mean().backward()
+    assert torch.allclose(gr.float(), W.grad.float(), rtol=1e-2, atol=1e-6)
+    # eval mode goes through the fused path and records nothing
+    m.eval()
+    assert len(probs) == 1
