@@ -832,7 +832,10 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   PPMOE_CHECK_CUDA(cudaGetLastError());
 
   // ---- experts
-  const int grid = (int)std::min<long long>(nsm, W.max_tiles);
+  // persistent grids: every SM, less the SMs left free for concurrent communication kernels
+  // (expert-parallel callers set PPMOE_PREFILL_FREE_SMS so NCCL transfers overlap the GEMMs)
+  static const int free_sms = [] { const char* v = getenv("PPMOE_PREFILL_FREE_SMS"); return v ? atoi(v) : 0; }();
+  const int grid = (int)std::min<long long>(std::max(1, nsm - free_sms), W.max_tiles);
   GUArgs ga{static_cast<const __nv_bfloat16*>(x), H, G, xpitch, tile_expert, tile_row0, ntiles, pair_token, pair_w,
             reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status, 0};
   // stages of (2 A tiles + B) that fit in 227 KB of shared memory: 5 up to G = 32, 4 at
