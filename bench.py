@@ -342,6 +342,53 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def profile_ep(args, world, rank, local):
+    """Config 5 per-phase times: for each chunk count, 3 warm-up calls, 5 calls with
+    ExpertParallelMoE.profile (median per phase), then 10 timed calls (max over ranks)."""
+    import torch.distributed as tdist
+    P = importlib.import_module(PKG)
+    ep = importlib.import_module(PKG + ".ep")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        tdist.init_process_group("nccl", device_id=dev)
+    L = P.synth.make_layer(0, H, E, G, router_scale=1.75)
+    m = P.TauSparseMoE(H, E * G, E, G, 0.70).to(dev)
+    P.physical_reorder_for_inference(m, L.gate_w, L.up_w, L.down_w, L.router_w, F.one_hot(L.experts_id, E).t(), 0.70)
+    epm = ep.ExpertParallelMoE(m.W_gate, m.W_up, m.W_down, m.router, E, G, 0.70,
+                               logit_bias=P.synth.zipf_bias(E, 1.2).to(dev))
+    n = 65536 // world
+    x = P.synth.make_tokens(5, 65536, H)[rank * n:(rank + 1) * n].to(dev)
+    keys = ["route_plan", "count_exchange_and_dispatch_enqueue", "experts_and_transfers", "combine"]
+    for ch in [int(c) for c in args.profile_ep.split(",")]:
+        epm.chunks = ch
+        for _ in range(3):
+            epm(x)
+        epm.profile = True
+        st = []
+        for _ in range(5):
+            epm(x)
+            st.append(dict(epm.last_stats))
+        epm.profile = False
+        torch.cuda.synchronize()
+        if world > 1:
+            tdist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            epm(x)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 10], device=dev)
+        if world > 1:
+            tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        print(json.dumps({"rank": rank, "ranks": world, "chunks": ch, "ms_per_call_max_over_ranks": t.item(),
+                          "phases_ms": {k: sorted(s_[k] for s_ in st)[2] for k in keys},
+                          "sent_rows": st[-1]["sent_rows"], "recv_rows": st[-1]["recv_rows"]}), flush=True)
+    if world > 1:
+        tdist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -356,6 +403,9 @@ def main():
                     help="only run 3 prefill calls of this many tokens (for ncu captures) and exit")
     ap.add_argument("--profile-decode", type=int, default=0,
                     help="only run 3 decode calls of this many tokens on 8 layers (for ncu captures) and exit")
+    ap.add_argument("--profile-ep", default="",
+                    help="comma-separated chunk counts: print config-5 expert-parallel phase times "
+                         "(CUDA events on the calling stream, per rank) for each and exit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
 
@@ -364,6 +414,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile_ep:
+        profile_ep(args, world, rank, local)
         return
     if args.profile_prefill:
         P = importlib.import_module(PKG)
@@ -530,8 +583,16 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_ms = t.item()
         return e2e_ms * 1e3 / (e2e_steps * args.layers)
+    xdev = [x.to(dev).view(1, 1, H) for x in xh]
+
+    def module_device_step():  # the module call alone: activations already on the device
+        with torch.cuda.stream(stream):
+            for l, m in enumerate(mods):
+                m(xdev[l])
+
     e2e_us = timed(e2e_abi_step)
     e2e_module_us = timed(e2e_module_step)
+    module_device_us = timed(module_device_step)
     mods[0].check_device_status()
 
     batched = {str(n): bench_decode_batch(P, dev, mods, n, max(3, args.steps // 2), args.warmup, stream)
@@ -562,7 +623,9 @@ def main():
                     "d2h_bytes_per_step": args.layers * H * 2,
                     "path": "C-ABI ppmoe_decode_host per layer (pinned host x in, host out back; entry point bound once)",
                     "module_us_per_layer": e2e_module_us,
-                    "module_path": "TauSparseMoE.forward, eager, pinned host x .to(cuda), out copy_ to host"},
+                    "module_path": "TauSparseMoE.forward, eager, pinned host x .to(cuda), out copy_ to host",
+                    "module_device_us_per_layer": module_device_us,
+                    "module_device_path": "TauSparseMoE.forward, eager, x resident on the device (no copies)"},
             "gpu_launches": args.steps * args.layers,
             "decode_batched": batched,
             "prefill": pre,

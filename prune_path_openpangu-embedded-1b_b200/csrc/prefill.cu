@@ -315,6 +315,7 @@ constexpr int kGUMaxStages = 5;  // cp.async groups kept in flight per producer 
 struct GUPairArgs {
   GUArgs g;
   const int* unit_tile;  // per unit: first tile * 2 + (1 if the unit has a second tile)
+  int nsplit;            // 1, or 2: each unit's neurons in two halves run as separate units
 };
 
 __global__ void __launch_bounds__(800, 1)
@@ -324,7 +325,8 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.stages, LAG = S - 2;
-  const int NB = 2 * a.G;
+  const int NS = pa.nsplit, GS = a.G / NS;  // neurons per (split) unit
+  const int NB = 2 * GS;
   const uint32_t a_bytes = kTileM * 128, b_bytes = (uint32_t)NB * 128;
   const uint32_t stage_bytes = 2 * a_bytes + b_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * stage_bytes);
@@ -333,7 +335,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
   uint64_t* tempty = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 1);
   const int KB = a.H / kBK;
-  const int nunits = a.ntiles[1];
+  const int nunits = a.ntiles[1] * NS;  // unit u: tile pair u / NS, neuron half u % NS
   if (tid == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 257); mbar_init(&empty[s], 1); }
     mbar_init(tfull, 1);
@@ -354,7 +356,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     uint8_t* const a_base = smem + h * a_bytes;
     int it = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-      const int ut = pa.unit_tile[u], t0 = ut >> 1;
+      const int ut = pa.unit_tile[u / NS], t0 = ut >> 1, nh = u % NS;
       const int e = a.tile_expert[t0];
       // padding rows and the absent second tile load nothing: their stale shared-memory rows
       // only reach accumulator rows that the epilogue discards
@@ -374,7 +376,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
         cp_async_commit();
         if (pr == 0) {
           mbar_arrive_expect_tx(&full[s], b_bytes);
-          tma_load_3d(smem + s * stage_bytes + 2 * a_bytes, &mapGU, kb * kBK, 0, e * a.G, &full[s]);
+          tma_load_3d(smem + s * stage_bytes + 2 * a_bytes, &mapGU, kb * kBK, 0, e * a.G + nh * GS, &full[s]);
         }
         if (it >= LAG) {
           if (LAG == 3) cp_async_wait<3>(); else if (LAG == 2) cp_async_wait<2>(); else cp_async_wait<1>();
@@ -390,7 +392,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
     int it = 0, ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
-      const bool two = pa.unit_tile[u] & 1;
+      const bool two = pa.unit_tile[u / NS] & 1;
       mbar_wait_parked(tempty, (ul & 1) ^ 1, a.status);
       tc_fence_after();
       for (int kb = 0; kb < KB; ++kb, ++it) {
@@ -414,13 +416,13 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     const int cmid = NB / 64 * 32, cbeg = cw ? cmid : 0, cend = cw ? NB : cmid;  // this warp's columns
     int ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
-      const int ut = pa.unit_tile[u];
+      const int ut = pa.unit_tile[u / NS], nh = u % NS;
       mbar_wait_parked(tfull, ul & 1, a.status);
       tc_fence_after();
       if (h == 0 || (ut & 1)) {
         const int p = a.tile_row0[(ut >> 1) + h] + r;
         const float wg = a.pair_w[p];
-        __nv_bfloat16* orow = a.a2 + (size_t)p * a.G;
+        __nv_bfloat16* orow = a.a2 + (size_t)p * a.G + nh * GS;
         for (int c0 = cbeg; c0 < cend; c0 += 32) {
           float v[32];
           tmem_ld32(tmem + h * 256 + ((uint32_t)(q * 32) << 16) + c0, v);
@@ -456,6 +458,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
 // ======================================================================== down GEMM + combine
 struct DownArgs {
   int H, G, NCW;
+  int NGRP;  // units per tile: tile t's column chunks in NGRP consecutive groups (small batches)
   float* ypart;  // [pairs][H] fp32
   const int* tile_expert;
   const int* tile_row0;
@@ -487,8 +490,8 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 1024));
-  const int NCH = a.H / a.NCW;
-  const int ntiles = *a.ntiles;
+  const int NCH = a.H / a.NCW, NCG = NCH / a.NGRP;
+  const int nunits = *a.ntiles * a.NGRP;
   if (tid == 0) {
     for (int s = 0; s < kDownStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
     mbar_init(afull, 1);
@@ -504,12 +507,13 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
 
   if (warp == 4 && lane == 0) {  // TMA producer
     int tl = 0, ch = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+    for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
+      const int tile = un / a.NGRP, cb = (un % a.NGRP) * NCG;
       const int e = a.tile_expert[tile], row0 = a.tile_row0[tile];
       mbar_wait_parked(aempty, (tl & 1) ^ 1, a.status);
       mbar_arrive_expect_tx(afull, a_bytes);
       for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + kb * a_kb, &mapA2, kb * kBK, row0, afull);
-      for (int c = 0; c < NCH; ++c, ++ch) {
+      for (int c = cb; c < cb + NCG; ++c, ++ch) {
         const int s = ch % kDownStages;
         mbar_wait_parked(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
         mbar_arrive_expect_tx(&bfull[s], b_bytes);
@@ -520,10 +524,10 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   } else if (warp == 5 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
     int tl = 0, ch = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+    for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
       mbar_wait_parked(afull, tl & 1, a.status);
       tc_fence_after();
-      for (int c = 0; c < NCH; ++c, ++ch) {
+      for (int c = 0; c < NCG; ++c, ++ch) {
         const int s = ch % kDownStages, acc = ch & 1;
         mbar_wait_parked(&tempty[acc], ((ch >> 1) & 1) ^ 1, a.status);
         mbar_wait_parked(&bfull[s], (ch / kDownStages) & 1, a.status);
@@ -550,9 +554,10 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     const int r = warp * 32 + lane;
     uint8_t* stg0 = stg;  // 2 x (16 KB + 8 KB), 1024-byte aligned
     int ch = 0, sub = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    for (int un = blockIdx.x; un < nunits; un += gridDim.x) {
+      const int tile = un / a.NGRP, cb = (un % a.NGRP) * NCG;
       const int row0 = a.tile_row0[tile];
-      for (int c = 0; c < NCH; ++c, ++ch) {
+      for (int c = cb; c < cb + NCG; ++c, ++ch) {
         const int acc = ch & 1;
         mbar_wait_parked(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
@@ -764,6 +769,14 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   // ---- router GEMM + selection
   const int EP = (E + 15) / 16 * 16;
   CUtensorMap mX, mR, mGU, mA2, mD;
+  // Batches of a few hundred tokens (about one or two 128-row tiles per expert) give the
+  // grouped GEMMs fewer work units than SMs.  There each gate/up unit is split into two neuron
+  // halves and each down tile into column groups, so that more SMs stream the experts' weights
+  // (measured 3-4% faster from 128 to 1,024 tokens; slower below 128 tokens, where every
+  // kernel is latency-bound and the extra units only add work).
+  static const int small_split = [] { const char* v = getenv("PPMOE_SMALL_SPLIT"); return v ? atoi(v) : 1; }();
+  const bool small = small_split && N > 128 && N <= 1024;
+  const int gu_split = small && G % 32 == 0 ? 2 : 1;
   {
     cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)N}, s[1] = {(cuuint64_t)H * 2};
     cuuint32_t b[2] = {kBK, kTileM};
@@ -785,7 +798,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   }
   {
     cuuint64_t d[3] = {(cuuint64_t)H, 2, (cuuint64_t)E * G}, s[2] = {(cuuint64_t)H * 2, (cuuint64_t)H * 6};
-    cuuint32_t b[3] = {kBK, 2, (cuuint32_t)G};
+    cuuint32_t b[3] = {kBK, 2, (cuuint32_t)(G / gu_split)};
     if ((rc = make_map(&mGU, pk + PL.experts, 3, d, s, b))) return rc;
   }
   {
@@ -840,8 +853,8 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
             reinterpret_cast<__nv_bfloat16*>(ws + W.a2), status, 0};
   // stages of (2 A tiles + B) that fit in 227 KB of shared memory: 5 up to G = 32, 4 at
   // G = 96, 3 at G = 128
-  const size_t pair_stage = 2 * kTileM * 128 + (size_t)2 * G * 128;
-  GUPairArgs pa{ga, reinterpret_cast<const int*>(ws + W.unit_tile)};
+  const size_t pair_stage = 2 * kTileM * 128 + (size_t)2 * (G / gu_split) * 128;
+  GUPairArgs pa{ga, reinterpret_cast<const int*>(ws + W.unit_tile), gu_split};
   pa.g.stages = (int)std::min<size_t>(kGUMaxStages, (232448 - 1024 - 256) / pair_stage);
   const size_t p_smem = 1024 + (size_t)pa.g.stages * pair_stage + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p_smem));
@@ -856,7 +869,9 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     if ((rc = make_map_2d(&mYh, y_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_128B, d, sh, b))) return rc;
     if ((rc = make_map_2d(&mYl, y_lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_64B, d, sl, b))) return rc;
   }
-  DownArgs da{H, G, NCW, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
+  const int NCH = H / NCW;
+  const int ngrp = !small ? 1 : NCH % 3 == 0 ? 3 : NCH % 2 == 0 ? 2 : 1;
+  DownArgs da{H, G, NCW, ngrp, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
   const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
