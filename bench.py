@@ -449,6 +449,13 @@ def main():
                 m.forward_decode(x)
         torch.cuda.synchronize()
         ms[0].check_device_status()
+        # union of selected experts per layer (launch order above: layers 0-7, three times)
+        ks = []
+        for m in ms:
+            w = torch.empty(args.profile_decode, E, dtype=torch.bfloat16, device=dev)
+            m.forward_decode(x, weights_out=w)
+            ks.append(int((w > 0).any(0).sum()))
+        print(json.dumps({"profile_decode_union_experts_per_layer": ks}), flush=True)
         return
     dist = None
     if world > 1:

@@ -61,6 +61,8 @@ struct DecodeArgs {
   int pdl;
   int x_host;  // x is pinned, device-mapped host memory: plain loads instead of a bulk copy
   unsigned long long* trace;  // optional per-CTA phase timestamps [grid][32] (diagnostics)
+  float pf_thr;  // one token: L2-prefetch the records of experts with probability >= pf_thr (0: off;
+                 // default 1 / E, PPMOE_DECODE_PF scales it)
 };
 
 __device__ __forceinline__ unsigned long long clk64() {  // diagnostics stamp: global ns timer
@@ -307,8 +309,51 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   // one warp per token
   if constexpr (CTASEL) {  // one token, E <= 64 (chosen on the host)
     float w[kMaxExpertsPerLane];
-    const uint32_t bits =
-        select_one_token_cta<kDecWarps>(lg, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf));
+    constexpr int kSelWarps = kDecWarps - 2;
+    uint32_t bits = 0;
+    if (warp >= kSelWarps) {
+      // Speculative L2 prefetch while the other warps select: the records of every expert
+      // whose probability reaches pf_thr (a superset of the selection), each CTA a contiguous
+      // 1/grid share of the candidates' bytes in 16 KB pieces.  The copies issued after the
+      // selection then read L2 instead of waiting on HBM.
+      if (a.pf_thr > 0.f) {
+        float l2[2];
+        uint32_t mk = 0u;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          l2[r] = lane + 32 * r < E ? lg[lane + 32 * r] : -INFINITY;
+          if (lane + 32 * r < E) mk = max(mk, float_order_key(l2[r]));
+        }
+        const float m = float_from_order_key(__reduce_max_sync(0xffffffffu, mk));
+        float ex[2], sm = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          ex[r] = lane + 32 * r < E ? expf(l2[r] - m) : 0.f;
+          sm += ex[r];
+        }
+        sm = warp_sum(sm);
+        const float lim = a.pf_thr * sm;
+        const uint32_t c0 = __ballot_sync(0xffffffffu, ex[0] >= lim), c1 = __ballot_sync(0xffffffffu, ex[1] >= lim);
+        const int nc = __popc(c0) + __popc(c1);
+        const uint32_t rec = 6u * (uint32_t)H * (uint32_t)G;  // bytes of one expert's records
+        const uint32_t piece = 16384u, ppe = (rec + piece - 1) / piece;
+        const int total = nc * (int)ppe, P = gridDim.x;
+        const int b0 = (int)((long long)total * blockIdx.x / P), b1 = (int)((long long)total * (blockIdx.x + 1) / P);
+        for (int k = b0 + (warp - kSelWarps) * 32 + lane; k < b1; k += 64) {
+          int ci = k / (int)ppe;
+          const uint32_t off = (uint32_t)(k % (int)ppe) * piece;
+          // ci-th set bit of (c1:c0), ascending expert order
+          int e;
+          if (ci < __popc(c0)) e = __fns(c0, 0, ci + 1);
+          else e = 32 + __fns(c1, 0, ci - __popc(c0) + 1);
+          const uint32_t sz = min(piece, rec - off);
+          const char* src = reinterpret_cast<const char*>(a.experts) + (size_t)e * rec + off;
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(sz) : "memory");
+        }
+      }
+    } else {
+      bits = select_one_token_cta<kSelWarps>(lg, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf));
+    }
     if (warp == 0) {
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
@@ -1031,6 +1076,10 @@ int decode_launch(const void* x, int tokens, const void* packed, int H, int E, i
   a.pdl = pdl;
   a.x_host = x_host;
   a.trace = g_trace;
+  {
+    static const float pf = [] { const char* v = getenv("PPMOE_DECODE_PF"); return v ? (float)atof(v) : 1.f; }();
+    a.pf_thr = (tokens == 1 && E <= 64) ? pf / (float)E : 0.f;
+  }
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];

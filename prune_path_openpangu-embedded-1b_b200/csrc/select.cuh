@@ -271,7 +271,7 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
 // warp computes the softmax keys redundantly (identical code, identical results); warp w
 // ranks experts (w % 2) * 32 + lane against the experts of part w / 2 (NW / 2 parts), the
 // partial ranks and mass sums meet in shared memory, and warp 0 finishes.  Same exactness
-// condition and fallback as select_rank.  All NW warps of the CTA must call it.
+// condition and fallback as select_rank.  Warps 0 .. NW-1 of the CTA must all call it.
 // scratch: 2 * (NW / 2) * 64 words of shared memory.  Returns the kept-expert bitmask of
 // slot i (expert lane + 32 i) in warp 0 (other warps: 0) and writes w (warp 0 only valid).
 template <int NW>
@@ -320,7 +320,8 @@ __device__ __forceinline__ uint32_t select_one_token_cta(const float* lg, int E,
     prank[p * 64 + h * 32 + lane] = rk;
     psum[p * 64 + h * 32 + lane] = S;
   }
-  __syncthreads();
+  // the NW calling warps only (other warps of the CTA may be busy elsewhere)
+  asm volatile("bar.sync 3, %0;" ::"n"(NW * 32) : "memory");
   uint32_t bits = 0;
   if (warp == 0) {
     float Sr[2];
