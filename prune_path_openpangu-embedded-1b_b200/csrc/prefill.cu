@@ -130,13 +130,28 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
       if (t < a.N) {
+        if (c0 + 32 <= a.E && a.E % 8 == 0 && (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) {
+          // whole 32-expert chunk: four 16-byte stores
+          uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int e = c0 + j;
-          if (e < a.E) {
-            float l = bf16r(v[j]);
-            if (a.bias) l = bf16r(l + a.bias[e]);
-            a.logits[(size_t)t * a.E + e] = __float2bfloat16_rn(l);
+          for (int j = 0; j < 32; j += 2) {
+            float l0 = bf16r(v[j]), l1 = bf16r(v[j + 1]);
+            if (a.bias) { l0 = bf16r(l0 + a.bias[c0 + j]); l1 = bf16r(l1 + a.bias[c0 + j + 1]); }
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(l0, l1);
+            pk[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(a.logits + (size_t)t * a.E + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int e = c0 + j;
+            if (e < a.E) {
+              float l = bf16r(v[j]);
+              if (a.bias) l = bf16r(l + a.bias[e]);
+              a.logits[(size_t)t * a.E + e] = __float2bfloat16_rn(l);
+            }
           }
         }
       }
@@ -175,64 +190,78 @@ __global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, in
   }
 }
 
-// One CTA: per-expert prefix over token blocks, 128-padded expert offsets, tile list,
-// padding rows, activation counts.
-__global__ void scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E, int* __restrict__ blockoff,
-                            int* __restrict__ count, int* __restrict__ exp_off, int* __restrict__ ntiles,
-                            int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ unit_tile,
-                            int* __restrict__ pair_token, float* __restrict__ pair_w,
+// One CTA of 1024 threads: per-expert prefix over token blocks, 128-padded expert offsets,
+// tile list, gate/up units, padding rows, activation counts.  Warp w owns experts w, w + 32,
+// ...: its lanes scan the expert's block counts 32 at a time (warp shuffles); warp 0 scans
+// the experts' tile and unit counts.
+__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E,
+                            int* __restrict__ blockoff, int* __restrict__ count, int* __restrict__ exp_off,
+                            int* __restrict__ ntiles, int* __restrict__ tile_expert, int* __restrict__ tile_row0,
+                            int* __restrict__ unit_tile, int* __restrict__ pair_token, float* __restrict__ pair_w,
                             long long* __restrict__ act_counts) {
   __shared__ int off_s[257];
   __shared__ int uoff_s[257];
   __shared__ int cnt_s[256];
-  const int e = threadIdx.x;
-  int run = 0;
-  if (e < E) {
-    for (int b0 = 0; b0 < nblocks; b0 += 8) {  // eight independent loads in flight
-      int c[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int e = warp; e < E; e += nw) {
+    int carry = 0;
+    for (int b0 = 0; b0 < nblocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int v = b < nblocks ? blockcnt[(size_t)b * E + e] : 0;
+      int inc = v;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) c[q] = b0 + q < nblocks ? blockcnt[(size_t)(b0 + q) * E + e] : 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (b0 + q < nblocks) {
-          blockoff[(size_t)(b0 + q) * E + e] = run;
-          run += c[q];
-        }
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      if (b < nblocks) blockoff[(size_t)b * E + e] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
     }
-    count[e] = run;
-    cnt_s[e] = run;
-    if (act_counts) act_counts[e] += run;
+    if (lane == 0) {
+      count[e] = carry;
+      cnt_s[e] = carry;
+      if (act_counts) act_counts[e] += carry;
+    }
   }
   __syncthreads();
-  if (e == 0) {
-    int o = 0, u = 0;
-    for (int q = 0; q < E; ++q) {
-      off_s[q] = o;
-      uoff_s[q] = u;
-      const int t = (cnt_s[q] + kTileM - 1) / kTileM;
-      o += t * kTileM;
-      u += (t + 1) / 2;
+  if (warp == 0) {  // exclusive prefixes of the padded rows and of the units, in expert order
+    int orow = 0, ou = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int t = e < E ? (cnt_s[e] + kTileM - 1) / kTileM : 0;
+      int it = t, iu = (t + 1) / 2;
+      const int t0 = it, u0 = iu;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, it, o), z = __shfl_up_sync(0xffffffffu, iu, o);
+        if (lane >= o) { it += y; iu += z; }
+      }
+      if (e < E) {
+        off_s[e] = orow + (it - t0) * kTileM;
+        uoff_s[e] = ou + (iu - u0);
+      }
+      orow += __shfl_sync(0xffffffffu, it, 31) * kTileM;
+      ou += __shfl_sync(0xffffffffu, iu, 31);
     }
-    off_s[E] = o;
-    ntiles[0] = o / kTileM;
-    ntiles[1] = u;
+    if (lane == 0) {
+      off_s[E] = orow;
+      ntiles[0] = orow / kTileM;
+      ntiles[1] = ou;
+    }
   }
   __syncthreads();
-  if (e < E) {
-    const int o = off_s[e];
-    exp_off[e] = o;
-    const int padded = off_s[e + 1] - o;
-    for (int i = 0; i < padded / kTileM; ++i) {
+  for (int e = warp; e < E; e += nw) {
+    const int o = off_s[e], t = (off_s[e + 1] - o) / kTileM;
+    if (lane == 0) exp_off[e] = o;
+    for (int i = lane; i < t; i += 32) {
       tile_expert[o / kTileM + i] = e;
       tile_row0[o / kTileM + i] = o + i * kTileM;
     }
     // gate/up work units: consecutive tile pairs of one expert (first tile * 2 + has-second)
-    const int t = padded / kTileM;
-    for (int i = 0; i < t; i += 2) unit_tile[uoff_s[e] + i / 2] = (o / kTileM + i) * 2 + (i + 1 < t);
+    for (int i = 2 * lane; i < t; i += 64) unit_tile[uoff_s[e] + i / 2] = (o / kTileM + i) * 2 + (i + 1 < t);
+    // padding rows of the expert's last tile
+    for (int p = o + cnt_s[e] + lane; p < off_s[e + 1]; p += 32) { pair_token[p] = -1; pair_w[p] = 0.f; }
   }
-  // padding rows of every expert's last tile, spread over the whole block
-  for (int q = 0; q < E; ++q)
-    for (int p = off_s[q] + cnt_s[q] + e; p < off_s[q + 1]; p += blockDim.x) { pair_token[p] = -1; pair_w[p] = 0.f; }
 }
 
 // Per token block: (token, expert) pairs in token order within each expert.
@@ -241,7 +270,7 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
                                float* __restrict__ pair_w, int* __restrict__ tok_pairs, int* __restrict__ tok_k) {
   // The block's 256 gate-weight rows are consecutive in memory: one coalesced copy into shared
   // memory (row pitch E + 2 elements against bank conflicts), plus each token's selection
-  // bitmask.  Warp w owns experts w, w + 8, ... and walks the 8 token chunks in order, so each
+  // bitmask.  Warp w owns experts w, w + (warps), ... and walks the 8 token chunks in order, so each
   // pair's slot is a running ballot prefix; the token-side index (its pairs in expert order)
   // comes from the bitmask.
   extern __shared__ __align__(16) uint8_t sc_smem[];
@@ -250,7 +279,8 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
   uint32_t* bm = reinterpret_cast<uint32_t*>(sc_smem + (size_t)256 * P * 2);  // [256][8]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
-  for (int i = tid; i < nt * E / 2; i += 256) {  // rows wpitch elements apart (E when dense)
+  const int nw = blockDim.x >> 5;
+  for (int i = tid; i < nt * E / 2; i += blockDim.x) {  // rows wpitch elements apart (E when dense)
     const int r = (2 * i) / E, c = (2 * i) % E;
     *reinterpret_cast<uint32_t*>(ws + r * P + c) =
         *reinterpret_cast<const uint32_t*>(w + (size_t)(t0 + r) * wpitch + c);
@@ -268,7 +298,7 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
     tok_k[t0 + tid] = k;
   }
   __syncthreads();
-  for (int e = warp; e < E; e += 8) {
+  for (int e = warp; e < E; e += nw) {
     int run = exp_off[e] + blockoff[(size_t)blockIdx.x * E + e];
     for (int c = 0; c < 8; ++c) {
       const int r = c * 32 + lane;
@@ -788,7 +818,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
   }
   if (mode == kPrefillRouteOnly) {  // router GEMM + selection only: the router rows alone are read
-    const int rstages = EP <= 128 ? 6 : 4;
+    const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;
     RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
     const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
     PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
@@ -814,7 +844,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   }
 
   if (mode != kPrefillExperts) {
-  const int rstages = EP <= 128 ? 6 : 4;  // stages in flight, within the shared-memory budget
+  const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;  // stages in flight, within the shared-memory budget
   RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
   const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
@@ -838,9 +868,9 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sc_smem + 256 * 8 * 4)));
   count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, wpitch, N, E, blockcnt);
-  scan_kernel<<<1, 256, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
+  scan_kernel<<<1, 1024, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
                                  reinterpret_cast<int*>(ws + W.unit_tile), pair_token, pair_w, reinterpret_cast<long long*>(counts));
-  scatter_kernel<<<W.nblocks, 256, sc_smem + 256 * 8 * 4, st>>>(weights, wpitch, N, E, blockoff, exp_off, pair_token, pair_w,
+  scatter_kernel<<<W.nblocks, 512, sc_smem + 256 * 8 * 4, st>>>(weights, wpitch, N, E, blockoff, exp_off, pair_token, pair_w,
                                                        reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
   PPMOE_CHECK_CUDA(cudaGetLastError());
 
@@ -922,7 +952,7 @@ int route_launch(const void* x, int N, const void* packed, int H, int E, int G, 
     cuuint32_t b[2] = {kBK, (cuuint32_t)EP};
     if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
   }
-  const int rstages = EP <= 128 ? 6 : 4;
+  const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;
   RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
   const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));

@@ -6,6 +6,7 @@
 
 namespace ppmoe {
 
+template <int EPL>  // experts per lane: E <= 32 EPL
 __global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, int N, int E, float tau_b,
                                     const float* __restrict__ bias, __nv_bfloat16* __restrict__ w_out,
                                     uint8_t* __restrict__ mask_out, __nv_bfloat16* __restrict__ probs_out) {
@@ -18,37 +19,37 @@ __global__ void route_logits_kernel(const __nv_bfloat16* __restrict__ logits, in
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = lane + 32 * i;
     float v = -INFINITY;
-    if (e < E) {
+    if (i < EPL && e < E) {
       v = __bfloat162float(logits[(size_t)t * E + e]);
       if (bias) v = bf16r(v + bias[e]);
     }
     l[i] = v;
   }
-  const uint32_t bits = select_experts_warp(l, E, tau_b, w, kbuf[threadIdx.x >> 5]);
+  const uint32_t bits = select_experts_warp<EPL>(l, E, tau_b, w, kbuf[threadIdx.x >> 5]);
   if (probs_out) {
     // training-mode output y_soft = softmax(logits) (src/MoEBlock.py:68, 93-94), computed with
     // the operations the selection uses, so these are exactly the probabilities it ranked
     uint32_t mk = 0u;
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i)
+    for (int i = 0; i < EPL; ++i)
       if (lane + 32 * i < E) mk = max(mk, float_order_key(l[i]));
     const float m = float_from_order_key(__reduce_max_sync(0xffffffffu, mk));
     float ex[kMaxExpertsPerLane], sum = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-      ex[i] = (lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
+      ex[i] = (i < EPL && lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
       sum += ex[i];
     }
     sum = warp_sum(sum);
     const float rs = __frcp_rn(sum);
 #pragma unroll
-    for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+    for (int i = 0; i < EPL; ++i) {
       const int e = lane + 32 * i;
       if (e < E) probs_out[(size_t)t * E + e] = __float2bfloat16_rn(bf16r(__fmul_rn(ex[i], rs)));
     }
   }
 #pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i) {
+  for (int i = 0; i < EPL; ++i) {
     const int e = lane + 32 * i;
     if (e < E) {
       w_out[(size_t)t * E + e] = __float2bfloat16_rn(w[i]);
@@ -127,7 +128,8 @@ int route_logits_launch(const void* logits, int N, int E, float tau, const float
                         uint8_t* mask_out, cudaStream_t st, void* probs_out) {
   if (N == 0) return PPMOE_OK;
   const int warps = 8;
-  route_logits_kernel<<<(N + warps - 1) / warps, warps * 32, 0, st>>>(
+  auto kern = E <= 64 ? route_logits_kernel<2> : route_logits_kernel<kMaxExpertsPerLane>;
+  kern<<<(N + warps - 1) / warps, warps * 32, 0, st>>>(
       static_cast<const __nv_bfloat16*>(logits), N, E, __bfloat162float(__float2bfloat16_rn(tau)), bias,
       static_cast<__nv_bfloat16*>(w_out), mask_out, static_cast<__nv_bfloat16*>(probs_out));
   PPMOE_CHECK_CUDA(cudaGetLastError());

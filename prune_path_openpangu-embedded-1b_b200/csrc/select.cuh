@@ -218,21 +218,24 @@ __device__ __forceinline__ bool select_rank(const uint32_t (&key)[kMaxExpertsPer
 // lane + 32*i was selected.  Each probability is a bf16 value, so its fp32 bit pattern has
 // 16 zero low bits; the 32-bit key (bf16 bits of p) << 16 | (0xFFFF - e) orders candidates
 // by p descending and then by expert index ascending.
+template <int EPL = kMaxExpertsPerLane>
 __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExpertsPerLane], int E,
                                                         float tau_b, float (&w)[kMaxExpertsPerLane],
                                                         uint32_t* kbuf, bool throughput = false,
                                                         uint32_t* keys_out = nullptr) {
+  // EPL < kMaxExpertsPerLane: the caller guarantees E <= 32 * EPL, and only the first EPL
+  // slots are touched (the rest are compile-time zeros), so the code for larger E is not built
   const int lane = threadIdx.x & 31;
   uint32_t mk = 0u;
 #pragma unroll
-  for (int i = 0; i < kMaxExpertsPerLane; ++i)
+  for (int i = 0; i < EPL; ++i)
     if (lane + 32 * i < E) mk = max(mk, float_order_key(l[i]));
   const float m = float_from_order_key(__reduce_max_sync(0xffffffffu, mk));
   float ex[kMaxExpertsPerLane];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
-    ex[i] = (lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
+    ex[i] = (i < EPL && lane + 32 * i < E) ? expf(l[i] - m) : 0.f;
     s += ex[i];
   }
   s = warp_sum(s);
@@ -241,7 +244,7 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i) {
     const int e = lane + 32 * i;
-    if (e < E) {
+    if (i < EPL && e < E) {
       const float p = bf16r(__fmul_rn(ex[i], rs));  // p >= 0: its bit pattern orders like p
       key[i] = (__float_as_uint(p) & 0xFFFF0000u) | (0xFFFFu - static_cast<uint32_t>(e));
     } else {
@@ -252,9 +255,11 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   bool done;
   // throughput: the bitonic network (O(E log E) work) instead of the rank count (O(E^2)
   // work, lower latency); measured slower for 16 tokens in the fused decode, so off there.
-  if (E <= 32) done = throughput ? select_parallel<1>(key, E, tau_b, bits) : select_rank<1>(key, E, tau_b, bits, kbuf);
-  else if (E <= 64) done = throughput ? select_parallel<2>(key, E, tau_b, bits) : select_rank<2>(key, E, tau_b, bits, kbuf);
-  else if (E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
+  if (EPL == 1 || (EPL > 1 && E <= 32))
+    done = throughput ? select_parallel<1>(key, E, tau_b, bits) : select_rank<1>(key, E, tau_b, bits, kbuf);
+  else if (EPL == 2 || (EPL > 2 && E <= 64))
+    done = throughput ? select_parallel<2>(key, E, tau_b, bits) : select_rank<2>(key, E, tau_b, bits, kbuf);
+  else if (EPL <= 4 || E <= 128) done = select_parallel<4>(key, E, tau_b, bits);
   else done = select_parallel<8>(key, E, tau_b, bits);
   if (keys_out) {
 #pragma unroll
@@ -263,7 +268,7 @@ __device__ __forceinline__ uint32_t select_experts_warp(const float (&l)[kMaxExp
   if (!done) bits = select_sequential(key, E, tau_b);
 #pragma unroll
   for (int i = 0; i < kMaxExpertsPerLane; ++i)
-    w[i] = (bits >> i) & 1u ? bf16r(__frcp_rn(1.f + expf(-l[i]))) : 0.f;
+    w[i] = (i < EPL && ((bits >> i) & 1u)) ? bf16r(__frcp_rn(1.f + expf(-l[i]))) : 0.f;
   return bits;
 }
 
