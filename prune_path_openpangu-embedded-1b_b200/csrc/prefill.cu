@@ -12,11 +12,12 @@
 //                                             two 128-row tiles x the expert's interleaved
 //                                             gate/up rows, SwiGLU and gate weight in the
 //                                             epilogue -> a2 rows) + down_gemm_kernel (a2 x
-//                                             down_t, one 24-bit-float row per pair) +
+//                                             down_t, one scaled-fp16 row per pair) +
 //                                             pair_combine_kernel (per token, its rows in
 //                                             expert order)
 // Numerics follow the reference's bf16 rounding points; the per-token combine over experts
 // accumulates in fp32 and rounds once (the reference Triton kernel adds bf16 atomics).
+#include <cuda_fp16.h>
 #include <mutex>
 #include "umma.cuh"
 
@@ -57,7 +58,9 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   w.pair_token = take((size_t)w.max_pairs * 4);
   w.pair_w = take((size_t)w.max_pairs * 4);
   w.a2 = take((size_t)w.max_pairs * G * 2);
-  w.ypart = take((size_t)w.max_pairs * H * 3);  // 24-bit down-projection row of every pair (2 planes)
+  // down-projection row of every pair: fp16 values [pairs][H], then one int8 power-of-two
+  // scale per 64-column slice [pairs][H / 64]
+  w.ypart = take((size_t)w.max_pairs * H * 2 + align_up((size_t)w.max_pairs * (H / 64), 1024));
   w.tok_pairs = take((size_t)N * E * 4);        // per token: its pairs in expert order
   w.tok_k = take((size_t)N * 4);
   w.total = o;
@@ -489,7 +492,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
 struct DownArgs {
   int H, G, NCW;
   int NGRP;  // units per tile: tile t's column chunks in NGRP consecutive groups (small batches)
-  float* ypart;  // [pairs][H] fp32
+  int8_t* yscale;  // [pairs][H / 64] exponent s of each slice's scale 2^s
   const int* tile_expert;
   const int* tile_row0;
   const int* ntiles;
@@ -501,8 +504,7 @@ constexpr int kDownStages = 2;
 
 __global__ void __launch_bounds__(192, 1)
 down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
-                 const __grid_constant__ CUtensorMap mapYh, const __grid_constant__ CUtensorMap mapYl,
-                 const DownArgs a) {
+                 const __grid_constant__ CUtensorMap mapYh, const DownArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(smem_raw), 1024));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -573,16 +575,16 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
       }
       umma_commit(aempty);
     }
-  } else if (warp < 4) {  // epilogue: the tile's rows, stored in pair order as 24-bit floats
-    // Each fp32 value is rounded to its top 24 bits (sign, exponent, 15 mantissa bits; relative
-    // error <= 2^-16) and split into a bf16 high plane and an 8-bit low plane, 3/4 of the
-    // fp32 bytes.  Per 64-column slice every thread writes its row into two swizzled staging
-    // tiles ([128 x 128 B] with the 128-byte swizzle, [128 x 64 B] with the 64-byte swizzle;
-    // both conflict-free), the 4 epilogue warps meet at a named barrier, and one thread stores
-    // both with TMA tensor stores (one bulk group).  Two staging pairs alternate; a pair is
-    // rewritten only after its stores have read it.
+  } else if (warp < 4) {  // epilogue: the tile's rows, stored in pair order as scaled fp16
+    // Per 64-column slice of a row: s = 14 - exponent(max |v|) (clamped), the values scaled by
+    // 2^s (exact) and rounded to fp16 (relative error <= 2^-11; |v 2^s| < 2^15, inside fp16's
+    // range whatever the magnitudes), s stored beside the row.  Every thread writes its row of
+    // the slice into a swizzled staging tile ([128 x 128 B], 128-byte swizzle, conflict-free),
+    // the 4 epilogue warps meet at a named barrier, and one thread stores the tile with a TMA
+    // tensor store.  Two staging tiles alternate; a tile is rewritten only after its store has
+    // read it.
     const int r = warp * 32 + lane;
-    uint8_t* stg0 = stg;  // 2 x (16 KB + 8 KB), 1024-byte aligned
+    const int S64 = a.H / 64;
     int ch = 0, sub = 0;
     for (int un = blockIdx.x; un < nunits; un += gridDim.x) {
       const int tile = un / a.NGRP, cb = (un % a.NGRP) * NCG;
@@ -592,38 +594,36 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
         mbar_wait_parked(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
         for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
-          uint8_t* hb = stg0 + (sub & 1) * 24576;
-          uint8_t* lb = hb + 16384;
+          uint8_t* hb = stg + (sub & 1) * 16384;
           if (r == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);  // the buffers are free
+          named_bar_sync(1, 128);  // the buffer is free
+          float v[2][32];
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v[0]);
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32, v[1]);
+          float m = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) m = fmaxf(m, fmaxf(fabsf(v[0][i]), fabsf(v[1][i])));
+          int sc = m > 0.f ? 14 - ((int)((__float_as_uint(m) >> 23) & 255u) - 127) : 0;
+          sc = max(-126, min(126, sc));
+          const float mul = __uint_as_float((uint32_t)(sc + 127) << 23);
+          a.yscale[(size_t)(row0 + r) * S64 + (c * a.NCW + c0) / 64] = (int8_t)sc;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            float v[32];
-            tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32 * half, v);
-            uint32_t u[32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(v[i]) + 0x80u;  // round at bit 8
-#pragma unroll
-            for (int j = 0; j < 4; ++j)  // high plane: 8 bf16 per 16-byte chunk
-              *reinterpret_cast<uint4*>(hb + sw128_offset(r, 4 * half + j)) =
-                  make_uint4(__byte_perm(u[8 * j], u[8 * j + 1], 0x7632), __byte_perm(u[8 * j + 2], u[8 * j + 3], 0x7632),
-                             __byte_perm(u[8 * j + 4], u[8 * j + 5], 0x7632), __byte_perm(u[8 * j + 6], u[8 * j + 7], 0x7632));
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {  // low plane: 16 bytes per chunk
-              uint32_t w4[4];
+            for (int j = 0; j < 4; ++j) {
+              uint32_t pk[4];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const int b = 16 * j + 4 * q;
-                w4[q] = __byte_perm(__byte_perm(u[b], u[b + 1], 0x0051), __byte_perm(u[b + 2], u[b + 3], 0x0051), 0x5410);
+                __half2 h2 = __floats2half2_rn(v[half][8 * j + 2 * q] * mul, v[half][8 * j + 2 * q + 1] * mul);
+                pk[q] = *reinterpret_cast<uint32_t*>(&h2);
               }
-              *reinterpret_cast<uint4*>(lb + sw64_offset(r, 2 * half + j)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+              *reinterpret_cast<uint4*>(hb + sw128_offset(r, 4 * half + j)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
           }
           fence_proxy_async();
-          named_bar_sync(1, 128);  // the tiles are complete
+          named_bar_sync(1, 128);  // the tile is complete
           if (r == 0) {
             tma_store_2d(&mapYh, hb, c * a.NCW + c0, row0);
-            tma_store_2d(&mapYl, lb, c * a.NCW + c0, row0);
             bulk_commit();
           }
         }
@@ -640,23 +640,28 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   }
 }
 
-// Per token: the rows of its pairs (24-bit floats: bf16 high plane + 8-bit low plane) added
-// in expert order in fp32 (deterministic), rounded once to bf16 (or written as fp32 partial
-// sums for expert-parallel ranks).  Thread c owns columns 8c .. 8c + 7.
-__device__ __forceinline__ void unpack24(uint32_t h0, uint32_t h1, uint32_t l, float* f) {
-  f[0] = __uint_as_float((h0 << 16) | ((l & 0xFFu) << 8));
-  f[1] = __uint_as_float((h0 & 0xFFFF0000u) | (l & 0xFF00u));
-  f[2] = __uint_as_float((h1 << 16) | ((l >> 8) & 0xFF00u));
-  f[3] = __uint_as_float((h1 & 0xFFFF0000u) | ((l >> 16) & 0xFF00u));
+// Per token: the rows of its pairs (scaled fp16, one power-of-two scale per 64-column slice)
+// added in expert order in fp32 (deterministic), rounded once to bf16 (or written as fp32
+// partial sums for expert-parallel ranks).  Thread c owns columns 8c .. 8c + 7.
+__device__ __forceinline__ void unpack_h8(const uint4 h, int sc, float* f) {
+  const float inv = __uint_as_float((uint32_t)(127 - sc) << 23);  // 2^-s, exact
+  const __half2* p = reinterpret_cast<const __half2*>(&h);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __half22float2(p[i]);
+    f[2 * i] = t.x * inv;
+    f[2 * i + 1] = t.y * inv;
+  }
 }
 
 template <bool F32OUT>
-__global__ void pair_combine_kernel(const uint4* __restrict__ yhi, const uint2* __restrict__ ylo,
+__global__ void pair_combine_kernel(const uint4* __restrict__ yv, const int8_t* __restrict__ ysc,
                                     const int* __restrict__ tok_pairs, const int* __restrict__ tok_k, int E, int H8,
                                     void* __restrict__ out) {
   __shared__ int rows[256];
   const int t = blockIdx.x;
   const int k = tok_k[t];
+  const int S64 = H8 / 8;
   for (int j = threadIdx.x; j < k; j += blockDim.x) rows[j] = tok_pairs[(size_t)t * E + j];
   __syncthreads();
   for (int c = threadIdx.x; c < H8; c += blockDim.x) {
@@ -666,29 +671,23 @@ __global__ void pair_combine_kernel(const uint4* __restrict__ yhi, const uint2* 
     int j = 0;
     for (; j + 4 <= k; j += 4) {  // four rows' loads in flight, added in order
       uint4 h[4];
-      uint2 l[4];
+      int sc[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const size_t o = (size_t)rows[j + q] * H8 + c;
-        h[q] = yhi[o];
-        l[q] = ylo[o];
+        h[q] = yv[(size_t)rows[j + q] * H8 + c];
+        sc[q] = ysc[(size_t)rows[j + q] * S64 + (c >> 3)];
       }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float f[8];
-        unpack24(h[q].x, h[q].y, l[q].x, f);
-        unpack24(h[q].z, h[q].w, l[q].y, f + 4);
+        unpack_h8(h[q], sc[q], f);
 #pragma unroll
         for (int i = 0; i < 8; ++i) s[i] += f[i];
       }
     }
     for (; j < k; ++j) {
-      const size_t o = (size_t)rows[j] * H8 + c;
-      const uint4 h = yhi[o];
-      const uint2 l = ylo[o];
       float f[8];
-      unpack24(h.x, h.y, l.x, f);
-      unpack24(h.z, h.w, l.y, f + 4);
+      unpack_h8(yv[(size_t)rows[j] * H8 + c], ysc[(size_t)rows[j] * S64 + (c >> 3)], f);
 #pragma unroll
       for (int i = 0; i < 8; ++i) s[i] += f[i];
     }
@@ -890,34 +889,32 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p_smem));
   gu_gemm_pair_kernel<<<grid, 800, p_smem, st>>>(mGU, pa);
   PPMOE_CHECK_CUDA(cudaGetLastError());
-  CUtensorMap mYh, mYl;
-  uint8_t* y_hi = ws + W.ypart;
-  uint8_t* y_lo = y_hi + (size_t)W.max_pairs * H * 2;
+  CUtensorMap mYh;
+  uint8_t* y_v = ws + W.ypart;
+  int8_t* y_sc = reinterpret_cast<int8_t*>(y_v + (size_t)W.max_pairs * H * 2);
   {
-    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)W.max_pairs}, sh[1] = {(cuuint64_t)H * 2}, sl[1] = {(cuuint64_t)H};
+    cuuint64_t d[2] = {(cuuint64_t)H, (cuuint64_t)W.max_pairs}, sh[1] = {(cuuint64_t)H * 2};
     cuuint32_t b[2] = {64, kTileM};
-    if ((rc = make_map_2d(&mYh, y_hi, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, CU_TENSOR_MAP_SWIZZLE_128B, d, sh, b))) return rc;
-    if ((rc = make_map_2d(&mYl, y_lo, CU_TENSOR_MAP_DATA_TYPE_UINT8, CU_TENSOR_MAP_SWIZZLE_64B, d, sl, b))) return rc;
+    if ((rc = make_map_2d(&mYh, y_v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_128B, d, sh, b))) return rc;
   }
   const int NCH = H / NCW;
   const int ngrp = !small ? 1 : NCH % 3 == 0 ? 3 : NCH % 2 == 0 ? 2 : 1;
-  DownArgs da{H, G, NCW, ngrp, reinterpret_cast<float*>(ws + W.ypart), tile_expert, tile_row0, ntiles, pair_token, status};
+  DownArgs da{H, G, NCW, ngrp, y_sc, tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
   const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
-                        2 * 24576 + 1024;
+                        2 * 16384 + 1024;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, mYl, da);
+  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   int* tok_pairs = reinterpret_cast<int*>(ws + W.tok_pairs);
   int* tok_k = reinterpret_cast<int*>(ws + W.tok_k);
-  const uint4* yh = reinterpret_cast<const uint4*>(y_hi);
-  const uint2* yl = reinterpret_cast<const uint2*>(y_lo);
+  const uint4* yh = reinterpret_cast<const uint4*>(y_v);
   const int H8 = H / 8, cthreads = std::min(256, (H8 + 31) / 32 * 32);
   if (mode == kPrefillExperts)
-    pair_combine_kernel<true><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);
+    pair_combine_kernel<true><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
   else
-    pair_combine_kernel<false><<<N, cthreads, 0, st>>>(yh, yl, tok_pairs, tok_k, E, H8, out);
+    pair_combine_kernel<false><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
 }
