@@ -351,7 +351,11 @@ struct GUPairArgs {
   int nsplit;            // 1, or 2: each unit's neurons in two halves run as separate units
 };
 
-__global__ void __launch_bounds__(800, 1)
+constexpr int kGUEpi = 16;                       // epilogue warps (8 or 16; 8 with 16 producers: 584 vs 562 us at config 3)
+constexpr int kGUProd = 8;                       // producer warps (gathers), half per tile (8 or 16)
+constexpr int kGUThreads = 32 * (kGUEpi + kGUProd + 1);  // + 1 MMA warp
+
+__global__ void __launch_bounds__(kGUThreads, 1)
 gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs pa) {
   const GUArgs& a = pa.g;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -370,22 +374,23 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
   const int KB = a.H / kBK;
   const int nunits = a.ntiles[1] * NS;  // unit u: tile pair u / NS, neuron half u % NS
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 257); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 32 * kGUProd + 1); mbar_init(&empty[s], 1); }
     mbar_init(tfull, 1);
-    mbar_init(tempty, 512);
+    mbar_init(tempty, 32 * kGUEpi);
     fence_mbar_init();
   }
-  if (warp == 24) tmem_alloc(tmem_slot, 512);
+  if (warp == kGUEpi + kGUProd) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 16 && warp < 24) {  // producers: gathered token rows; B via TMA
-    // Producer warp pw fills rows (pw % 4) * 32 .. + 31 of tile pw / 4.  Per instruction its
-    // 32 lanes copy the 128-byte k-slices of 4 rows (8 lanes per row, one 16-byte chunk each),
-    // so every copy instruction reads 4 whole 128-byte lines.
-    const int pr = tid - 512, pw = warp - 16, h = pw >> 2, rbase = (pw & 3) * 32, sub = lane >> 3, ck = lane & 7;
+  if (warp >= kGUEpi && warp < kGUEpi + kGUProd) {  // producers: gathered token rows; B via TMA
+    // Producer warp pw fills RPW consecutive rows of tile pw / WPT.  Per instruction its 32
+    // lanes copy the 128-byte k-slices of 4 rows (8 lanes per row, one 16-byte chunk each), so
+    // every copy instruction reads 4 whole 128-byte lines.
+    constexpr int WPT = kGUProd / 2, RPW = kTileM / WPT, NI = RPW / 4;
+    const int pr = tid - 32 * kGUEpi, pw = warp - kGUEpi, h = pw / WPT, rbase = (pw % WPT) * RPW, sub = lane >> 3, ck = lane & 7;
     uint8_t* const a_base = smem + h * a_bytes;
     int it = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
@@ -393,9 +398,9 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
       const int e = a.tile_expert[t0];
       // padding rows and the absent second tile load nothing: their stale shared-memory rows
       // only reach accumulator rows that the epilogue discards
-      const __nv_bfloat16* src[8];
+      const __nv_bfloat16* src[NI];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < NI; ++i) {
         const int tok = (h == 0 || (ut & 1)) ? a.pair_token[a.tile_row0[t0 + h] + rbase + 4 * i + sub] : -1;
         src[i] = tok >= 0 ? a.x + (size_t)tok * a.xpitch + ck * 8 : nullptr;
       }
@@ -404,7 +409,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
         mbar_wait_parked(&empty[s], ((it / S) & 1) ^ 1, a.status);
         uint8_t* st = a_base + s * stage_bytes;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < NI; ++i)
           if (src[i]) cp_async16(st + sw128_offset(rbase + 4 * i + sub, ck), src[i] + kb * kBK);
         cp_async_commit();
         if (pr == 0) {
@@ -421,7 +426,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     cp_async_wait<0>();
     fence_proxy_async();
     for (int j = max(0, it - LAG); j < it; ++j) mbar_arrive(&full[j % S]);
-  } else if (warp == 24 && lane == 0) {  // MMA issuer
+  } else if (warp == kGUEpi + kGUProd && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, NB);
     int it = 0, ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
@@ -444,9 +449,11 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
       }
       umma_commit(tfull);
     }
-  } else if (warp < 16) {  // epilogue: row r of tile h = pair; SwiGLU with the reference's rounding points
-    const int h = warp >> 3, cw = (warp >> 2) & 1, q = warp & 3, r = q * 32 + lane;
-    const int cmid = NB / 64 * 32, cbeg = cw ? cmid : 0, cend = cw ? NB : cmid;  // this warp's columns
+  } else if (warp < kGUEpi) {  // epilogue: row r of tile h = pair; SwiGLU with the reference's rounding points
+    // 16 warps: tile w / 8, column half (w / 4) % 2, TMEM lane quarter w % 4; 8 warps: tile w / 4
+    constexpr int EPT = kGUEpi / 2;  // epilogue warps per tile
+    const int h = warp / EPT, cw = EPT == 8 ? (warp >> 2) & 1 : 0, q = warp & 3, r = q * 32 + lane;
+    const int cmid = EPT == 8 ? NB / 64 * 32 : NB, cbeg = cw ? cmid : 0, cend = cw ? NB : cmid;  // this warp's columns
     int ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
       const int ut = pa.unit_tile[u / NS], nh = u % NS;
@@ -482,7 +489,7 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     }
   }
   __syncthreads();
-  if (warp == 24) {
+  if (warp == kGUEpi + kGUProd) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -501,8 +508,10 @@ struct DownArgs {
 };
 
 constexpr int kDownStages = 2;
+constexpr int kDownEpiWarps = 8;  // two warpgroups, each converting alternate 64-column slices
+constexpr int kDownThreads = 32 * (kDownEpiWarps + 2);
 
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kDownThreads, 1)
 down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constant__ CUtensorMap mapD,
                  const __grid_constant__ CUtensorMap mapYh, const DownArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -528,16 +537,16 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     for (int s = 0; s < kDownStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
     mbar_init(afull, 1);
     mbar_init(aempty, 1);
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 32 * kDownEpiWarps); }
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc(tmem_slot, 512);
+  if (warp == kDownEpiWarps + 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4 && lane == 0) {  // TMA producer
+  if (warp == kDownEpiWarps && lane == 0) {  // TMA producer
     int tl = 0, ch = 0;
     for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
       const int tile = un / a.NGRP, cb = (un % a.NGRP) * NCG;
@@ -553,7 +562,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
           tma_load_2d(sB + s * b_bytes + kb * b_kb, &mapD, kb * kBK, e * a.H + c * a.NCW, &bfull[s]);
       }
     }
-  } else if (warp == 5 && lane == 0) {  // MMA issuer
+  } else if (warp == kDownEpiWarps + 1 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
     int tl = 0, ch = 0;
     for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
@@ -575,15 +584,17 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
       }
       umma_commit(aempty);
     }
-  } else if (warp < 4) {  // epilogue: the tile's rows, stored in pair order as scaled fp16
+  } else if (warp < kDownEpiWarps) {  // epilogue: the tile's rows, stored in pair order as scaled fp16
     // Per 64-column slice of a row: s = 14 - exponent(max |v|) (clamped), the values scaled by
     // 2^s (exact) and rounded to fp16 (relative error <= 2^-11; |v 2^s| < 2^15, inside fp16's
     // range whatever the magnitudes), s stored beside the row.  Every thread writes its row of
     // the slice into a swizzled staging tile ([128 x 128 B], 128-byte swizzle, conflict-free),
-    // the 4 epilogue warps meet at a named barrier, and one thread stores the tile with a TMA
-    // tensor store.  Two staging tiles alternate; a tile is rewritten only after its store has
-    // read it.
-    const int r = warp * 32 + lane;
+    // the warpgroup's 4 warps meet at a named barrier, and one thread stores the tile with a
+    // TMA tensor store.  Warpgroup hf takes slices hf, hf + 2, ... of each chunk (TMEM lane
+    // quarter = warp % 4) and alternates two staging tiles of its own; a tile is rewritten only
+    // after its store has read it.
+    const int hf = warp >> 2, wq = warp & 3, r = wq * 32 + lane;
+    constexpr int NWG = kDownEpiWarps / 4;
     const int S64 = a.H / 64;
     int ch = 0, sub = 0;
     for (int un = blockIdx.x; un < nunits; un += gridDim.x) {
@@ -593,13 +604,13 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
         const int acc = ch & 1;
         mbar_wait_parked(&tfull[acc], (ch >> 1) & 1, a.status);
         tc_fence_after();
-        for (int c0 = 0; c0 < a.NCW; c0 += 64, ++sub) {
-          uint8_t* hb = stg + (sub & 1) * 16384;
+        for (int c0 = 64 * hf; c0 < a.NCW; c0 += 64 * NWG, ++sub) {
+          uint8_t* hb = stg + (hf * 2 + (sub & 1)) * 16384;
           if (r == 0) bulk_wait_read<1>();
-          named_bar_sync(1, 128);  // the buffer is free
+          named_bar_sync(1 + hf, 128);  // the buffer is free
           float v[2][32];
-          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0, v[0]);
-          tmem_ld32(tmem + acc * 256 + ((uint32_t)(warp * 32) << 16) + c0 + 32, v[1]);
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(wq * 32) << 16) + c0, v[0]);
+          tmem_ld32(tmem + acc * 256 + ((uint32_t)(wq * 32) << 16) + c0 + 32, v[1]);
           float m = 0.f;
 #pragma unroll
           for (int i = 0; i < 32; ++i) m = fmaxf(m, fmaxf(fabsf(v[0][i]), fabsf(v[1][i])));
@@ -621,7 +632,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
             }
           }
           fence_proxy_async();
-          named_bar_sync(1, 128);  // the tile is complete
+          named_bar_sync(1 + hf, 128);  // the tile is complete
           if (r == 0) {
             tma_store_2d(&mapYh, hb, c * a.NCW + c0, row0);
             bulk_commit();
@@ -634,7 +645,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     if (r == 0) bulk_wait<0>();
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kDownEpiWarps + 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -887,7 +898,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   pa.g.stages = (int)std::min<size_t>(kGUMaxStages, (232448 - 1024 - 256) / pair_stage);
   const size_t p_smem = 1024 + (size_t)pa.g.stages * pair_stage + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(gu_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p_smem));
-  gu_gemm_pair_kernel<<<grid, 800, p_smem, st>>>(mGU, pa);
+  gu_gemm_pair_kernel<<<grid, kGUThreads, p_smem, st>>>(mGU, pa);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   CUtensorMap mYh;
   uint8_t* y_v = ws + W.ypart;
@@ -903,9 +914,9 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
   const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
-                        2 * 16384 + 1024;
+                        (kDownEpiWarps / 4) * 2 * 16384 + 1024;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
-  down_gemm_kernel<<<grid, 192, d_smem, st>>>(mA2, mD, mYh, da);
+  down_gemm_kernel<<<grid, kDownThreads, d_smem, st>>>(mA2, mD, mYh, da);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   int* tok_pairs = reinterpret_cast<int*>(ws + W.tok_pairs);
   int* tok_k = reinterpret_cast<int*>(ws + W.tok_k);
