@@ -194,8 +194,9 @@ PPMOE_API int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int
 
 /* Expert-parallel prefill, dispatch side (no reference counterpart: the reference runs on one
  * device; this replaces the host-side send-list construction around the NCCL all-to-all).
- * Destination rank d owns experts d, d + ranks, d + 2 ranks, ...; a token is sent to d when it
- * selected at least one of them (weights [tokens][experts] bf16, 0 = not selected).  The tokens
+ * Destination rank d owns, of each group of `ranks` consecutive experts g ranks .. g ranks +
+ * ranks - 1, expert g ranks + d for even g and g ranks + ranks - 1 - d for odd g (snake order);
+ * a token is sent to d when it selected at least one of them (weights [tokens][experts] bf16, 0 = not selected).  The tokens
  * go in `chunks` consecutive chunks of whole 256-token blocks (chunk c: blocks
  * [nb c / chunks, nb (c + 1) / chunks), nb = ceil(tokens / 256)).  `send` receives one payload
  * row of row_pitch bytes per (token, destination): hidden bf16 activations, then the token's
@@ -210,11 +211,22 @@ PPMOE_API int ppmoe_ep_dispatch(const void* x, const void* weights, int tokens, 
                                 size_t ws_bytes, void* stream);
 /* Expert-parallel prefill, expert side: ppmoe_prefill_experts over received payload rows
  * (ppmoe_ep_dispatch layout: activations, then the gate weights of this rank's `experts` local
- * experts) without unpacking them; out_f32 [rows][hidden] fp32 partial sums.  Workspace as
- * ppmoe_prefill_workspace_bytes(rows, ...).  Replaces moe_local/global_scan, moe_dispatch and
+ * experts) without unpacking them.  partial_format 0: out = [rows][hidden] fp32 partial sums;
+ * 1: out = rows of ppmoe_ep_partial_pitch(hidden) bytes in the scaled-fp16 format (each
+ * value's relative error <= 2^-11; half the bytes of fp32 rows on the way back).  Workspace
+ * as ppmoe_prefill_workspace_bytes(rows, ...).  Replaces moe_local/global_scan, moe_dispatch and
  * moe_fused_expert_kernel (tl:133-328, 566-604) on the expert-owning rank. */
 PPMOE_API int ppmoe_ep_experts(const void* payload, int rows, int row_pitch, const void* packed, int hidden,
-                               int experts, int group, float* out_f32, void* ws, size_t ws_bytes, void* stream);
+                               int experts, int group, int partial_format, void* out, void* ws, size_t ws_bytes,
+                               void* stream);
+/* Bytes per row of the scaled-fp16 partial format (ppmoe_ep_experts partial_format 1): hidden
+ * fp16 values, each 64-column slice multiplied by 2^s (exact) so that |value| < 2^15, then the
+ * hidden / 64 int8 exponents s; padded to 16 bytes.  0 if hidden is not a multiple of 64. */
+PPMOE_API size_t ppmoe_ep_partial_pitch(int hidden);
+/* Source side for scaled-fp16 partial rows: out[t] = bf16( sum over d of row_of[d][t]'s row,
+ * rescaled to fp32 ) with fp32 additions in rank order.  back: rows of `pitch` bytes. */
+PPMOE_API int ppmoe_ep_combine_f16s(const void* back, int pitch, const int32_t* row_of, int ranks, int tokens,
+                                    int hidden, void* out, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Fused decode that allocates nothing and takes no workspace: for callers that cannot call

@@ -50,8 +50,10 @@ SIGNATURES = {
     "ppmoe_ep_dispatch_workspace_bytes": (_c_size_t, [_c_int, _c_int]),
     "ppmoe_ep_dispatch": (_c_int, [_c_void_p, _c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_void_p, _c_int,
                                    _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
-    "ppmoe_ep_experts": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p,
-                                  _c_void_p, _c_size_t, _c_void_p]),
+    "ppmoe_ep_experts": (_c_int, [_c_void_p, _c_int, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_int,
+                                  _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
+    "ppmoe_ep_partial_pitch": (_c_size_t, [_c_int]),
+    "ppmoe_ep_combine_f16s": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_void_p, _c_void_p]),
     "ppmoe_prefill": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float, _c_void_p,
                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "ppmoe_decode_noalloc": (_c_int, [_c_void_p, _c_int, _c_void_p, _c_int, _c_int, _c_int, _c_float,

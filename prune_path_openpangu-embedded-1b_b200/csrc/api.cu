@@ -332,19 +332,28 @@ int ppmoe_prefill_experts(const void* x, int tokens, const void* packed, int hid
 }
 
 int ppmoe_ep_experts(const void* payload, int rows, int row_pitch, const void* packed, int hidden, int experts,
-                     int group, float* out_f32, void* ws, size_t ws_bytes, void* stream) {
+                     int group, int partial_format, void* out, void* ws, size_t ws_bytes, void* stream) {
   g_err[0] = 0;
-  if (int rc = prefill_checks("ppmoe_ep_experts", payload, rows, packed, hidden, experts, group, out_f32, ws))
+  if (int rc = prefill_checks("ppmoe_ep_experts", payload, rows, packed, hidden, experts, group, out, ws))
     return rc;
   const int need = (int)align_up((size_t)(hidden + experts) * 2, 16);
   if (row_pitch < need || row_pitch % 16 != 0) {
     set_error("ppmoe_ep_experts: row_pitch=%d must be a multiple of 16 and >= %d", row_pitch, need);
     return PPMOE_ERR_INVALID_ARG;
   }
+  if (partial_format != 0 && partial_format != 1) {
+    set_error("ppmoe_ep_experts: partial_format=%d (0 fp32 rows, 1 scaled fp16 rows)", partial_format);
+    return PPMOE_ERR_INVALID_ARG;
+  }
   const uint8_t* p = static_cast<const uint8_t*>(payload);
-  return prefill_launch(p, rows, packed, hidden, experts, group, 0.f, nullptr, out_f32, nullptr,
+  return prefill_launch(p, rows, packed, hidden, experts, group, 0.f, nullptr, out, nullptr,
                         const_cast<uint8_t*>(p + (size_t)hidden * 2), nullptr, ws, ws_bytes,
-                        static_cast<cudaStream_t>(stream), 2, row_pitch / 2, row_pitch / 2);
+                        static_cast<cudaStream_t>(stream), partial_format ? 3 : 2, row_pitch / 2, row_pitch / 2);
+}
+
+size_t ppmoe_ep_partial_pitch(int hidden) {
+  if (hidden <= 0 || hidden % 64 != 0) return 0;
+  return f16s_pitch(hidden);
 }
 
 size_t ppmoe_route_workspace_bytes(int tokens, int hidden, int experts, int group) {

@@ -40,6 +40,9 @@ struct PackedLayout {
 };
 
 __host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+// Bytes of one scaled-fp16 row of H values: H fp16 (each 64-column slice scaled by 2^s), then
+// the H / 64 int8 exponents s, padded to 16 bytes.
+__host__ __device__ inline size_t f16s_pitch(int H) { return align_up((size_t)H * 2 + (size_t)H / 64, 16); }
 
 __host__ __device__ inline PackedLayout packed_layout(int H, int E, int G) {
   PackedLayout L;

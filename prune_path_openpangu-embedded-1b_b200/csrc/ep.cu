@@ -1,6 +1,7 @@
 // Expert-parallel prefill, source side: add the partial rows that the expert-owning ranks
 // returned for each token (fp32, or bf16 in the reduced-traffic mode) in rank order with fp32
 // additions, and round once to bf16.
+#include <cuda_fp16.h>
 #include "common.cuh"
 
 namespace ppmoe {
@@ -41,8 +42,9 @@ __global__ void ep_combine_kernel(const T* __restrict__ back, const int* __restr
 
 
 // ------------------------------------------------------------------ dispatch
-// Destination d owns experts d, d + P, d + 2P, ...  A token goes to d when it selected at least
-// one of them (gate weight > 0).  The send buffer is chunk-major, then destination-major, tokens
+// Destination d owns, in expert group g (experts g P .. g P + P - 1), expert g P + d for even g
+// and g P + P - 1 - d for odd g (snake order: balanced under a prior that falls with the expert
+// index).  A token goes to d when it selected at least one of them (gate weight > 0).  The send buffer is chunk-major, then destination-major, tokens
 // ascending inside each (chunk, destination) segment; each payload row is the token's H bf16
 // activations followed by its gate weights for d's experts (owned order), padded to row_pitch
 // bytes.  Chunk c covers token blocks [nb c / C, nb (c + 1) / C) of 256 tokens.
@@ -50,10 +52,18 @@ constexpr int kEpBlock = 256;
 constexpr int kEpMaxRanks = 8;
 constexpr int kEpMaxChunks = 8;
 
+__host__ __device__ inline int ep_owner(int e, int P) {
+  const int g = e / P, i = e - g * P;
+  return (g & 1) ? P - 1 - i : i;
+}
+__host__ __device__ inline int ep_expert(int d, int j, int P) {  // destination d's j-th expert
+  return j * P + ((j & 1) ? P - 1 - d : d);
+}
+
 __device__ __forceinline__ uint32_t ep_dest_bits(const __nv_bfloat16* w, int E, int P) {
   uint32_t bits = 0;
   for (int e = 0; e < E; ++e)
-    if (__bfloat162float(w[e]) > 0.f) bits |= 1u << (e % P);
+    if (__bfloat162float(w[e]) > 0.f) bits |= 1u << ep_owner(e, P);
   return bits;
 }
 
@@ -128,8 +138,39 @@ __global__ void ep_scatter_kernel(const __nv_bfloat16* __restrict__ x, const __n
       uint8_t* row = send + (size_t)pos * pitch;
       for (int c = lane; c < H8; c += 32) reinterpret_cast<uint4*>(row)[c] = xr[c];
       for (int j = lane; j < el; j += 32)
-        reinterpret_cast<__nv_bfloat16*>(row + (size_t)H * 2)[j] = w[(size_t)tt * E + d + P * j];
+        reinterpret_cast<__nv_bfloat16*>(row + (size_t)H * 2)[j] = w[(size_t)tt * E + ep_expert(d, j, P)];
     }
+  }
+}
+
+// Scaled-fp16 partial rows (ppmoe_ep_experts partial_format 1): row d of token t at
+// back + row_of[d][t] * pitch; values fp16 scaled by 2^s per 64-column slice, s (int8) after the
+// H values.  Thread c owns columns 4c .. 4c + 3; fp32 sums in rank order, one bf16 rounding.
+__global__ void ep_combine_f16s_kernel(const uint8_t* __restrict__ back, int pitch, const int* __restrict__ row_of,
+                                       int P, int n, int H, uint2* __restrict__ out) {
+  const int t = blockIdx.x;
+  int rows[8];
+#pragma unroll
+  for (int d = 0; d < 8; ++d) rows[d] = d < P ? row_of[(size_t)d * n + t] : -1;
+  for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int d = 0; d < 8; ++d) {
+      if (rows[d] >= 0) {
+        const uint8_t* row = back + (size_t)rows[d] * pitch;
+        const uint2 v = reinterpret_cast<const uint2*>(row)[c];
+        const int sc = reinterpret_cast<const int8_t*>(row + (size_t)H * 2)[c >> 4];
+        const float inv = __uint_as_float((uint32_t)(127 - sc) << 23);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        s.x += a.x * inv; s.y += a.y * inv; s.z += b.x * inv; s.w += b.y * inv;
+      }
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(s.x, s.y), hi = __floats2bfloat162_rn(s.z, s.w);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<uint32_t*>(&hi);
+    out[(size_t)t * (H / 4) + c] = pk;
   }
 }
 
@@ -213,4 +254,24 @@ extern "C" int ppmoe_ep_combine(const float* back, const int32_t* row_of, int ra
 extern "C" int ppmoe_ep_combine_bf16(const void* back, const int32_t* row_of, int ranks, int tokens, int hidden,
                                      void* out, void* stream) {
   return ep_combine(back, true, row_of, ranks, tokens, hidden, out, stream);
+}
+
+extern "C" int ppmoe_ep_combine_f16s(const void* back, int pitch, const int32_t* row_of, int ranks, int tokens,
+                                     int hidden, void* out, void* stream) {
+  clear_error();
+  if (ranks < 1 || ranks > 8 || tokens < 0 || hidden <= 0 || hidden % 64 != 0 || pitch < (int)f16s_pitch(hidden) ||
+      pitch % 16 != 0) {
+    set_error("ppmoe_ep_combine_f16s: ranks=%d (1..8), tokens=%d, hidden=%d (multiple of 64), pitch=%d (>= %zu, "
+              "multiple of 16)", ranks, tokens, hidden, pitch, f16s_pitch(hidden > 0 ? hidden : 64));
+    return PPMOE_ERR_UNSUPPORTED;
+  }
+  if (tokens == 0) return PPMOE_OK;
+  if (!back || !row_of || !out) {
+    set_error("ppmoe_ep_combine_f16s: null pointer");
+    return PPMOE_ERR_INVALID_ARG;
+  }
+  ep_combine_f16s_kernel<<<tokens, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(back), pitch, row_of, ranks, tokens, hidden, static_cast<uint2*>(out));
+  PPMOE_CHECK_CUDA(cudaGetLastError());
+  return PPMOE_OK;
 }

@@ -665,10 +665,12 @@ __device__ __forceinline__ void unpack_h8(const uint4 h, int sc, float* f) {
   }
 }
 
-template <bool F32OUT>
+// OUT: 0 bf16 rows, 1 fp32 partial rows, 2 scaled-fp16 partial rows of `opitch` bytes (H fp16,
+// then H / 64 int8 slice exponents: the expert-parallel return format, f16s_pitch)
+template <int OUT>
 __global__ void pair_combine_kernel(const uint4* __restrict__ yv, const int8_t* __restrict__ ysc,
                                     const int* __restrict__ tok_pairs, const int* __restrict__ tok_k, int E, int H8,
-                                    void* __restrict__ out) {
+                                    void* __restrict__ out, int opitch = 0) {
   __shared__ int rows[256];
   const int t = blockIdx.x;
   const int k = tok_k[t];
@@ -702,10 +704,31 @@ __global__ void pair_combine_kernel(const uint4* __restrict__ yv, const int8_t* 
 #pragma unroll
       for (int i = 0; i < 8; ++i) s[i] += f[i];
     }
-    if (F32OUT) {
+    if (OUT == 1) {
       float4* o = static_cast<float4*>(out) + ((size_t)t * H8 + c) * 2;
       o[0] = make_float4(s[0], s[1], s[2], s[3]);
       o[1] = make_float4(s[4], s[5], s[6], s[7]);
+    } else if (OUT == 2) {
+      // the slice's 8 threads (aligned lane groups: H is a multiple of 64) agree on its scale
+      float m = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(s[i]));
+      const unsigned am = __activemask();
+      m = fmaxf(m, __shfl_xor_sync(am, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(am, m, 2));
+      m = fmaxf(m, __shfl_xor_sync(am, m, 4));
+      int sc = m > 0.f ? 14 - ((int)((__float_as_uint(m) >> 23) & 255u) - 127) : 0;
+      sc = max(-126, min(126, sc));
+      const float mul = __uint_as_float((uint32_t)(sc + 127) << 23);
+      uint8_t* row = static_cast<uint8_t*>(out) + (size_t)t * opitch;
+      uint32_t pk[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __half2 h2 = __floats2half2_rn(s[2 * i] * mul, s[2 * i + 1] * mul);
+        pk[i] = *reinterpret_cast<uint32_t*>(&h2);
+      }
+      reinterpret_cast<uint4*>(row)[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      if ((c & 7) == 0) reinterpret_cast<int8_t*>(row + (size_t)H8 * 16)[c >> 3] = (int8_t)sc;
     } else {
       uint32_t pk[4];
 #pragma unroll
@@ -779,7 +802,7 @@ size_t route_workspace_bytes(long long N, int E);
 // mode: kPrefillFull (router -> selection -> experts -> bf16 out), kPrefillRouteOnly (stop
 // after the gate weights), kPrefillExperts (gate weights given in weights_out; expert compute
 // only; `out` receives fp32 partial sums instead of bf16).
-enum { kPrefillFull = 0, kPrefillRouteOnly = 1, kPrefillExperts = 2 };
+enum { kPrefillFull = 0, kPrefillRouteOnly = 1, kPrefillExperts = 2, kPrefillExpertsF16s = 3 };
 
 int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G, float tau, const float* bias,
                    void* out, void* logits_out, void* weights_out, int64_t* counts, void* wsp, size_t ws_bytes,
@@ -853,7 +876,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
     if ((rc = make_map(&mD, pk + PL.down_t, 2, d, s, b))) return rc;
   }
 
-  if (mode != kPrefillExperts) {
+  if (mode != kPrefillExperts && mode != kPrefillExpertsF16s) {
   const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;  // stages in flight, within the shared-memory budget
   RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
   const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
@@ -923,9 +946,11 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   const uint4* yh = reinterpret_cast<const uint4*>(y_v);
   const int H8 = H / 8, cthreads = std::min(256, (H8 + 31) / 32 * 32);
   if (mode == kPrefillExperts)
-    pair_combine_kernel<true><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
+    pair_combine_kernel<1><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
+  else if (mode == kPrefillExpertsF16s)
+    pair_combine_kernel<2><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out, (int)f16s_pitch(H));
   else
-    pair_combine_kernel<false><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
+    pair_combine_kernel<0><<<N, cthreads, 0, st>>>(yh, y_sc, tok_pairs, tok_k, E, H8, out);
   PPMOE_CHECK_CUDA(cudaGetLastError());
   return PPMOE_OK;
 }

@@ -37,8 +37,13 @@ __all__ = ["ExpertParallelMoE", "dispatch_reference", "combine_partials", "chunk
 
 
 def owned_experts(E: int, world: int, rank: int) -> torch.Tensor:
-    """Experts of ``rank`` under the strided assignment: rank, rank + P, ..."""
-    return torch.arange(rank, E, world)
+    """Experts of ``rank`` under the snake assignment: in expert group g (experts g P ..
+    g P + P - 1) rank r owns g P + r for even g and g P + P - 1 - r for odd g.  Against a
+    router prior that falls with the expert index (the Zipf skew of the benchmark) every rank
+    gets one popular and one unpopular expert of each pair of groups, where a plain stride
+    (r, r + P, ...) gives rank 0 the most popular expert of every group."""
+    return torch.tensor([g * world + (rank if g % 2 == 0 else world - 1 - rank) for g in range(E // world)],
+                        dtype=torch.long)
 
 
 def chunk_bounds(n: int, chunks: int) -> list:
@@ -64,7 +69,8 @@ def dispatch_reference(x: torch.Tensor, weights: torch.Tensor, world: int, chunk
         raise ValueError(f"experts={E} not divisible by world size {world}")
     el = E // world
     b = chunk_bounds(n, chunks)
-    wv = weights.view(n, el, world).transpose(1, 2)  # [n, P, el]: expert d + P*j at [:, d, j]
+    perm = torch.stack([owned_experts(E, world, d) for d in range(world)]).to(weights.device)  # [P, el]
+    wv = weights[:, perm]  # [n, P, el]: destination d's experts in owned order
     sel = (wv > 0).any(-1)
     counts = torch.zeros(world, chunks, dtype=torch.int64)
     row_of = torch.full((world, n), -1, dtype=torch.int32)
@@ -87,11 +93,47 @@ def dispatch_reference(x: torch.Tensor, weights: torch.Tensor, world: int, chunk
     return send, counts, row_of
 
 
-def combine_partials(back: torch.Tensor, row_of: torch.Tensor, n: int) -> torch.Tensor:
+def f16s_pitch(H: int) -> int:
+    """Bytes per scaled-fp16 partial row (``ppmoe_ep_partial_pitch``)."""
+    return (2 * H + H // 64 + 15) // 16 * 16
+
+
+def f16s_encode(rows: torch.Tensor) -> torch.Tensor:
+    """Torch restatement of the scaled-fp16 row format (CPU ranks): per 64-column slice
+    s = 14 - exponent(max |v|) clamped to [-126, 126], fp16(v * 2^s), then the int8 exponents."""
+    n, H = rows.shape
+    v = rows.float().view(n, H // 64, 64)
+    m = v.abs().amax(-1)
+    e = torch.frexp(m)[1] - 1  # exponent of m (m = f 2^e, 1 <= f < 2)
+    sc = torch.where(m > 0, 14 - e, torch.zeros_like(e)).clamp(-126, 126)
+    h = (v * torch.exp2(sc.float())[..., None]).to(torch.float16).view(n, H)
+    out = torch.zeros(n, f16s_pitch(H), dtype=torch.uint8)
+    out[:, :2 * H] = h.view(torch.uint8)
+    out[:, 2 * H:2 * H + H // 64] = sc.to(torch.int8).view(torch.uint8)
+    return out
+
+
+def f16s_decode(rows: torch.Tensor, H: int) -> torch.Tensor:
+    """fp32 values of scaled-fp16 rows (exact rescaling)."""
+    n = rows.shape[0]
+    h = rows[:, :2 * H].contiguous().view(torch.float16).float().view(n, H // 64, 64)
+    sc = rows[:, 2 * H:2 * H + H // 64].contiguous().view(torch.int8).float()
+    return (h * torch.exp2(-sc)[..., None]).view(n, H)
+
+
+def combine_partials(back: torch.Tensor, row_of: torch.Tensor, n: int, H: Optional[int] = None) -> torch.Tensor:
     """Sum the partial rows of every token in rank order (fp32 additions) and round once to
     bf16: ``out[t] = bf16(sum_d back[row_of[d, t]])`` over the rows that exist (``ppmoe_ep_combine``
-    on CUDA; the same order with torch operations on CPU ranks)."""
+    on CUDA; the same order with torch operations on CPU ranks).  uint8 ``back`` holds
+    scaled-fp16 rows of hidden size ``H`` (``ppmoe_ep_combine_f16s``)."""
     P = row_of.shape[0]
+    if back.dtype == torch.uint8:
+        if back.is_cuda:
+            out = torch.empty(n, H, dtype=torch.bfloat16, device=back.device)
+            _lib.call("ppmoe_ep_combine_f16s", back.data_ptr(), back.shape[1], row_of.data_ptr(), P, n, H,
+                      out.data_ptr(), torch.cuda.current_stream(back.device).cuda_stream)
+            return out
+        back = f16s_decode(back, H)
     if back.is_cuda:
         out = torch.empty(n, back.shape[1], dtype=torch.bfloat16, device=back.device)
         fn = "ppmoe_ep_combine_bf16" if back.dtype == torch.bfloat16 else "ppmoe_ep_combine"
@@ -149,10 +191,12 @@ class ExpertParallelMoE:
         self.last_stats = {}
         self.profile = False  # record per-phase device times (ms) into last_stats
         self.chunks = 2 if self.world > 1 else 1  # pipeline depth (measured best at 2 on 2 GPUs)
-        # "fp32": partial sums cross the network in fp32 and the only bf16 rounding is the final
-        # one (the single-device numerics).  "bf16": each rank rounds its partial once before
-        # sending (half the combine traffic, a second rounding: looser tolerance).
-        self.partials = "fp32"
+        # Format of the partial sums that cross the network on the way back:
+        # "f16s" (default): fp16 with a power-of-two scale per 64-column slice, the prefill's
+        #   pair-row format (relative error <= 2^-11 per rank's partial, half the fp32 bytes);
+        # "fp32": the only rounding is the final bf16 one;
+        # "bf16": each rank rounds its partial once to bf16 (looser tolerance).
+        self.partials = "f16s"
 
     # ------------------------------------------------------------------ kernels
     def _route(self, x):
@@ -173,20 +217,26 @@ class ExpertParallelMoE:
                   _stream_handle(x.device))
         return w
 
-    def _experts(self, payload):
-        """Partial sums [rows, H] fp32 of this rank's experts over received payload rows."""
+    def _experts(self, payload, fmt: int = 0):
+        """Partial sums of this rank's experts over received payload rows: ``[rows, H]`` fp32
+        (``fmt`` 0), or rows of ``ppmoe_ep_partial_pitch(H)`` bytes in the scaled-fp16 format
+        (``fmt`` 1, uint8 ``[rows, pitch]``)."""
         n = payload.shape[0]
         if self.expert_fn is not None:
             v = payload.view(torch.bfloat16)
-            return self.expert_fn(v[:, :self.H], v[:, self.H:self.H + self.el],
+            part = self.expert_fn(v[:, :self.H], v[:, self.H:self.H + self.el],
                                   owned_experts(self.E, self.world, self.rank))
-        out = torch.empty(n, self.H, dtype=torch.float32, device=payload.device)
+            return part if fmt == 0 else f16s_encode(part)
+        if fmt == 0:
+            out = torch.empty(n, self.H, dtype=torch.float32, device=payload.device)
+        else:
+            out = torch.empty(n, _lib.load().ppmoe_ep_partial_pitch(self.H), dtype=torch.uint8, device=payload.device)
         if n == 0:
             return out
         m = self.local
         ws = m.prefill_workspace(n)
         _lib.call("ppmoe_ep_experts", payload.data_ptr(), n, payload.shape[1], m.packed().data_ptr(), self.H,
-                  self.el, self.G, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle(payload.device))
+                  self.el, self.G, fmt, out.data_ptr(), ws.data_ptr(), ws.numel(), _stream_handle(payload.device))
         return out
 
     def _dispatch(self, x, w, C, pitch):
@@ -259,15 +309,19 @@ class ExpertParallelMoE:
             recv.append(rx)
         mark()
         # experts per chunk, each followed by its return transfer into the chunk's rows of `back`
-        bf16_parts = getattr(self, "partials", "fp32") == "bf16"
-        back = torch.empty(sbase[C], self.H, dtype=torch.bfloat16 if bf16_parts else torch.float32,
-                           device=x.device)
+        mode = getattr(self, "partials", "f16s")
+        fmt = 1 if mode == "f16s" else 0
+        if fmt:
+            back = torch.empty(sbase[C], f16s_pitch(self.H), dtype=torch.uint8, device=x.device)
+        else:
+            back = torch.empty(sbase[C], self.H, dtype=torch.bfloat16 if mode == "bf16" else torch.float32,
+                               device=x.device)
         bworks = []
         for c in range(C):
             if P > 1:
                 works[c].wait()
-            part = self._experts(recv[c])
-            if bf16_parts:
+            part = self._experts(recv[c], fmt)
+            if mode == "bf16":
                 part = part.to(torch.bfloat16)
             if P == 1:
                 back[sbase[c]:sbase[c + 1]] = part
@@ -277,7 +331,7 @@ class ExpertParallelMoE:
         for wk in bworks:
             wk.wait()
         mark()
-        y = combine_partials(back, row_of, n)
+        y = combine_partials(back, row_of, n, self.H)
         mark()
         self.last_stats = {"sent_rows": sum(sum(v) for v in sc), "recv_rows": sum(sum(v) for v in rc),
                            "chunks": C}

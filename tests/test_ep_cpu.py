@@ -109,20 +109,21 @@ def test_dispatch_reference_and_combine_single_process():
     x = torch.arange(5 * 8, dtype=torch.float32).view(5, 8).to(torch.bfloat16)
     pitch = ep.row_pitch(8, 4)
     assert pitch == 32
+    # snake assignment at 2 ranks: rank 0 owns experts 0, 3, 4, 7; rank 1 owns 1, 2, 5, 6
+    assert ep.owned_experts(8, 2, 0).tolist() == [0, 3, 4, 7] and ep.owned_experts(8, 2, 1).tolist() == [1, 2, 5, 6]
     send, cnt, row_of = ep.dispatch_reference(x, w, 2, 1, pitch)
-    # rank 0 owns experts 0,2,4,6; rank 1 owns 1,3,5,7
-    assert cnt.tolist() == [[3], [3]]
-    assert row_of.tolist() == [[0, -1, -1, 1, 2], [3, -1, 4, -1, 5]]
+    assert cnt.tolist() == [[2], [2]]
+    assert row_of.tolist() == [[-1, -1, -1, 0, 1], [2, -1, 3, -1, -1]]
     v = send.view(torch.bfloat16)
-    assert torch.equal(v[:, :8], x[[0, 3, 4, 0, 2, 4]])
+    assert torch.equal(v[:, :8], x[[3, 4, 0, 2]])
     sw = v[:, 8:12].float()
-    assert sw[0].tolist() == [0.0, 0.0, 0.0, 0.25] and sw[1].tolist() == [0.75, 0.0, 0.0, 0.0]
-    assert sw[2].tolist() == [0.0, 0.0, 0.5, 0.0] and sw[3].tolist() == [0.5, 0.0, 0.0, 0.0]
-    assert sw[4].tolist() == [0.0, 0.0, 1.0, 0.0] and sw[5].tolist() == [0.0, 0.0, 0.0, 0.5]
-    back = torch.arange(6 * 3, dtype=torch.float32).view(6, 3)
+    assert sw[0].tolist() == [0.75, 0.0, 0.0, 0.0] and sw[1].tolist() == [0.0, 0.0, 0.5, 0.5]
+    assert sw[2].tolist() == [0.5, 0.0, 0.0, 0.25] and sw[3].tolist() == [0.0, 0.0, 1.0, 0.0]
+    back = torch.arange(4 * 3, dtype=torch.float32).view(4, 3)
     out = ep.combine_partials(back, row_of, 5)
-    assert out[0].float().tolist() == (back[0] + back[3]).tolist()
-    assert out[4].float().tolist() == (back[2] + back[5]).tolist()
+    assert out[0].float().tolist() == back[2].tolist()
+    assert out[4].float().tolist() == back[1].tolist()
+    assert out[3].float().tolist() == back[0].tolist()
     assert out[1].float().abs().sum() == 0
 
 
@@ -139,7 +140,7 @@ def test_dispatch_reference_chunks():
     for c in range(3):
         for d in range(4):
             k = int(cnt[d, c])
-            toks = [t for t in range(b[c], b[c + 1]) if bool((w[t, d::4] > 0).any())]
+            toks = [t for t in range(b[c], b[c + 1]) if bool((w[t, ep.owned_experts(16, 4, d)] > 0).any())]
             assert len(toks) == k
             assert row_of[d, toks].tolist() == list(range(pos, pos + k))
             pos += k

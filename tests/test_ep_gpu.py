@@ -140,3 +140,28 @@ def test_ep_two_gpus_nccl():
     y, ref, yb = res[0][1]
     assert_close_out(y, ref, "ep(2) vs single-device prefill")
     _close_loose(yb, ref, "ep(2) bf16 partials vs single-device prefill")
+
+
+def test_ep_partial_formats(cuda):
+    """The expert side's scaled-fp16 partial rows decode to the fp32 partial rows within fp16
+    precision of each 64-column slice's maximum, and the source-side combine of those rows
+    (ppmoe_ep_combine_f16s) equals the torch restatement bit for bit."""
+    from importlib import import_module
+    ep = import_module(pkg().__name__ + ".ep")
+    L = make_layer(15, 1536, 64, 96, 0.7)
+    epm, _ = _ep_module(L, 0.7, cuda)
+    x = pkg().synth.make_tokens(15, 700, 1536).to(cuda)
+    w = epm._route(x)
+    send, cnt, row_of = epm._dispatch(x, w, 1, ep.row_pitch(1536, 64))
+    rows = int(cnt.sum())
+    p32 = epm._experts(send[:rows], 0)
+    p16 = epm._experts(send[:rows], 1)
+    assert p16.shape[1] == ep.f16s_pitch(1536) == pkg()._lib.load().ppmoe_ep_partial_pitch(1536)
+    dec = ep.f16s_decode(p16.cpu(), 1536).view(rows, 24, 64)
+    ref = p32.cpu().view(rows, 24, 64)
+    bound = ref.abs().amax(-1, keepdim=True) * 2.0 ** -11
+    assert bool(((dec - ref).abs() <= bound).all())
+    assert torch.equal(ep.f16s_encode(p32.cpu()), p16.cpu())  # the restatement equals the kernel
+    y = ep.combine_partials(p16, row_of, 700, 1536).cpu()
+    y_ref = ep.combine_partials(p16.cpu(), row_of.cpu(), 700, 1536)
+    assert torch.equal(y, y_ref)
