@@ -4,9 +4,9 @@ The reference runs on one device only; this is the sharded form of its prefill p
 (``TauSparseMoE.forward_prefill``, src/tl_kernel_optimized_Ultimate_PanGU.py:532-604) for
 large token counts:
 
-* rank r owns experts ``r, r + P, r + 2P, ...`` (their packed gate/up/down records) and a
-  shard of the tokens; the strided assignment spreads popular low-index experts (skewed
-  routing) over all ranks instead of piling them on rank 0;
+* rank r owns one expert of every group of P consecutive experts in snake order
+  (``owned_experts``: their packed gate/up/down records) and a shard of the tokens; the snake
+  order balances skewed routing that favours low expert indices;
 * every rank routes its own tokens (``ppmoe_prefill_route``: tcgen05 router GEMM + selection);
 * a token row is sent once to each rank that owns at least one of its selected experts,
   together with its gate weights for that rank's experts, as one payload row: the send rows
@@ -14,8 +14,9 @@ large token counts:
   then a count exchange (``all_to_all_single`` of int64 counts, the one host synchronisation)
   and one payload ``all_to_all_single`` per chunk;
 * each rank runs its local experts on the received payload rows as they are
-  (``ppmoe_ep_experts``: grouped tcgen05 GEMMs) and returns fp32 partial sums with a second ``all_to_all_single`` (or bf16
-  partials in the optional reduced-traffic mode, ``partials="bf16"``);
+  (``ppmoe_ep_experts``: grouped tcgen05 GEMMs) and returns its partial sums with a second
+  ``all_to_all_single``: scaled-fp16 rows by default (``partials="f16s"``), or fp32 / bf16
+  rows (``partials="fp32"`` / ``"bf16"``);
 * the source adds the partials in rank order (deterministic) and rounds to bf16 once;
 * the tokens go through in chunks so that the all-to-all transfers of one chunk overlap the
   grouped GEMMs of its neighbours (see ``ExpertParallelMoE.__call__``).
