@@ -173,7 +173,10 @@ def bench_prefill(P, dev, steps, warmup):
             "unit": "tokens/s", "us_per_step": us, "steps": steps, "sum_k": k,
             "roofline_bound": "tensor", "achieved_tflops": flops / us / 1e6, "peak_tflops": peak[0],
             "roofline_frac": flops / us / 1e6 / peak[0], "peak_kind": peak[1], "flops_per_call": flops,
-            "l2": "each step writes/reads ~1 GB of dispatch scratch (> L2)"}
+            "roofline": {"bound": "tensor", "achieved": flops / us / 1e6, "peak": peak[0], "unit": "TFLOP/s",
+                         "frac": flops / us / 1e6 / peak[0], "peak_kind": peak[1],
+                         "flops_per_call": flops, "traffic": None},
+            "l2": "each step writes/reads ~0.7 GB of pair-row scratch (> L2)"}
 
 
 def bench_ep(P, dev, world, rank, steps, warmup, dist):
@@ -276,7 +279,18 @@ def bench_batch64(P, dev, mods, steps, warmup):
     torch.cuda.synchronize()
     mods[0].check_device_status()
     us = e0.elapsed_time(e1) * 1e3 / (steps * len(mods))
+    # algorithmic bytes: the union of the 64 tokens' experts (every expert here), router, x, out
+    ubytes = 0
+    for l, m in enumerate(mods):
+        w = torch.empty(64, E, dtype=torch.bfloat16, device=dev)
+        m.forward_prefill(xs[l], weights_out=w)
+        ubytes += int((w > 0).any(0).sum()) * EXPERT_BYTES + ROUTER_BYTES + 64 * IO_BYTES
+    gbs = ubytes / len(mods) / (us * 1e-6) / 1e9
+    peak = peaks()
     return {"tokens": 64, "us_per_layer": us, "tokens_per_s_per_layer": 64 / (us * 1e-6),
+            "union_bytes_per_layer": ubytes / len(mods), "achieved_gbs": gbs, "hbm_frac": gbs / peak[0],
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak[0], "unit": "GB/s", "frac": gbs / peak[0],
+                         "peak_kind": peak[1], "traffic": None},
             "path": "prefill kernels (more than 16 tokens)"}
 
 
