@@ -161,7 +161,8 @@ def test_ep_partial_formats(cuda):
     ref = p32.cpu().view(rows, 24, 64)
     bound = ref.abs().amax(-1, keepdim=True) * 2.0 ** -11
     assert bool(((dec - ref).abs() <= bound).all())
-    assert torch.equal(ep.f16s_encode(p32.cpu()), p16.cpu())  # the restatement equals the kernel
+    used = 2 * 1536 + 1536 // 64  # defined bytes of a row (the 16-byte padding is not written)
+    assert torch.equal(ep.f16s_encode(p32.cpu())[:, :used], p16.cpu()[:, :used])  # restatement == kernel
     y = ep.combine_partials(p16, row_of, 700, 1536).cpu()
     y_ref = ep.combine_partials(p16.cpu(), row_of.cpu(), 700, 1536)
     assert torch.equal(y, y_ref)
