@@ -166,3 +166,19 @@ def test_ep_partial_formats(cuda):
     y = ep.combine_partials(p16, row_of, 700, 1536).cpu()
     y_ref = ep.combine_partials(p16.cpu(), row_of.cpu(), 700, 1536)
     assert torch.equal(y, y_ref)
+
+
+@pytest.mark.parametrize("experts", [8, 16])
+def test_ep_local_layer_sizes_of_8_and_4_ranks(cuda, experts):
+    """A rank of 8-way (4-way) expert parallelism at E = 64 holds 8 (16) experts: the same
+    expert-side kernels on a layer of that many experts, against the oracle."""
+    L = make_layer(16, 1536, experts, 96, 0.7)
+    epm, m = _ep_module(L, 0.7, cuda)
+    x = pkg().synth.make_tokens(16, 600, 1536)
+    y = epm(x.to(cuda)).cpu()
+    lg = torch.empty(600, experts, dtype=torch.bfloat16, device=cuda)
+    w = torch.empty(600, experts, dtype=torch.bfloat16, device=cuda)
+    m.forward_prefill(x.to(cuda), logits_out=lg, weights_out=w)
+    ref = oracle().moe_mlp(x, L, 0.7, logits=lg.cpu())
+    assert_selection_matches(w.cpu(), lg.cpu(), 0.7, f"E={experts} selection")
+    assert_close_out(y, ref.out, f"ep(1) E={experts} vs oracle")
