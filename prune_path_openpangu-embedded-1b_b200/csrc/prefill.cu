@@ -393,17 +393,34 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     const int pr = tid - 32 * kGUEpi, pw = warp - kGUEpi, h = pw / WPT, rbase = (pw % WPT) * RPW, sub = lane >> 3, ck = lane & 7;
     uint8_t* const a_base = smem + h * a_bytes;
     int it = 0;
+    // padding rows and the absent second tile load nothing: their stale shared-memory rows
+    // only reach accumulator rows that the epilogue discards.  Unit u + grid's row pointers are
+    // loaded while unit u streams (three dependent global loads off the critical path).
+    auto unit_src = [&](int u, const __nv_bfloat16* (&src)[NI], int& e) {
+      e = 0;
+#pragma unroll
+      for (int i = 0; i < NI; ++i) src[i] = nullptr;
+      if (u >= nunits) return;
+      const int ut = pa.unit_tile[u / NS], t0 = ut >> 1;
+      e = a.tile_expert[t0];
+      if (h == 0 || (ut & 1)) {
+        const int row0 = a.tile_row0[t0 + h];
+#pragma unroll
+        for (int i = 0; i < NI; ++i) {
+          const int tok = a.pair_token[row0 + rbase + 4 * i + sub];
+          src[i] = tok >= 0 ? a.x + (size_t)tok * a.xpitch + ck * 8 : nullptr;
+        }
+      }
+    };
+    const __nv_bfloat16* nsrc[NI];
+    int ne;
+    unit_src(blockIdx.x, nsrc, ne);
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-      const int ut = pa.unit_tile[u / NS], t0 = ut >> 1, nh = u % NS;
-      const int e = a.tile_expert[t0];
-      // padding rows and the absent second tile load nothing: their stale shared-memory rows
-      // only reach accumulator rows that the epilogue discards
+      const int nh = u % NS, e = ne;
       const __nv_bfloat16* src[NI];
 #pragma unroll
-      for (int i = 0; i < NI; ++i) {
-        const int tok = (h == 0 || (ut & 1)) ? a.pair_token[a.tile_row0[t0 + h] + rbase + 4 * i + sub] : -1;
-        src[i] = tok >= 0 ? a.x + (size_t)tok * a.xpitch + ck * 8 : nullptr;
-      }
+      for (int i = 0; i < NI; ++i) src[i] = nsrc[i];
+      unit_src(u + gridDim.x, nsrc, ne);
       for (int kb = 0; kb < KB; ++kb, ++it) {
         const int s = it % S;
         mbar_wait_parked(&empty[s], ((it / S) & 1) ^ 1, a.status);
@@ -456,12 +473,15 @@ gu_gemm_pair_kernel(const __grid_constant__ CUtensorMap mapGU, const GUPairArgs 
     const int cmid = EPT == 8 ? NB / 64 * 32 : NB, cbeg = cw ? cmid : 0, cend = cw ? NB : cmid;  // this warp's columns
     int ul = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++ul) {
+      // the unit's rows and gate weights are known before its accumulators: load them first so
+      // that their latency overlaps the main loop
       const int ut = pa.unit_tile[u / NS], nh = u % NS;
+      const bool has = h == 0 || (ut & 1);
+      const int p = has ? a.tile_row0[(ut >> 1) + h] + r : 0;
+      const float wg = has ? a.pair_w[p] : 0.f;
       mbar_wait_parked(tfull, ul & 1, a.status);
       tc_fence_after();
-      if (h == 0 || (ut & 1)) {
-        const int p = a.tile_row0[(ut >> 1) + h] + r;
-        const float wg = a.pair_w[p];
+      if (has) {
         __nv_bfloat16* orow = a.a2 + (size_t)p * a.G + nh * GS;
         for (int c0 = cbeg; c0 < cend; c0 += 32) {
           float v[32];
