@@ -541,13 +541,13 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   const uint32_t a_kb = kTileM * 128;             // one 64-wide k-block of A
   const uint32_t b_kb = (uint32_t)a.NCW * 128;    // one 64-wide k-block of a B chunk
   const uint32_t a_bytes = KB2 * a_kb, b_bytes = KB2 * b_kb;
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + a_bytes;
+  uint8_t* sA = smem;  // two A tiles: the next tile's loads overlap this tile's chunks
+  uint8_t* sB = smem + 2 * a_bytes;
   uint64_t* bfull = reinterpret_cast<uint64_t*>(sB + kDownStages * b_bytes);
   uint64_t* bempty = bfull + kDownStages;
-  uint64_t* afull = bempty + kDownStages;
-  uint64_t* aempty = afull + 1;
-  uint64_t* tfull = aempty + 1;
+  uint64_t* afull = bempty + kDownStages;  // [2]
+  uint64_t* aempty = afull + 2;            // [2]
+  uint64_t* tfull = aempty + 2;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   uint8_t* stg = reinterpret_cast<uint8_t*>(align_up(reinterpret_cast<uintptr_t>(tempty + 2) + 16, 1024));
@@ -555,8 +555,7 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
   const int nunits = *a.ntiles * a.NGRP;
   if (tid == 0) {
     for (int s = 0; s < kDownStages; ++s) { mbar_init(&bfull[s], 1); mbar_init(&bempty[s], 1); }
-    mbar_init(afull, 1);
-    mbar_init(aempty, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&afull[i], 1); mbar_init(&aempty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 32 * kDownEpiWarps); }
     fence_mbar_init();
   }
@@ -571,9 +570,10 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
       const int tile = un / a.NGRP, cb = (un % a.NGRP) * NCG;
       const int e = a.tile_expert[tile], row0 = a.tile_row0[tile];
-      mbar_wait_parked(aempty, (tl & 1) ^ 1, a.status);
-      mbar_arrive_expect_tx(afull, a_bytes);
-      for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + kb * a_kb, &mapA2, kb * kBK, row0, afull);
+      const int ab = tl & 1;
+      mbar_wait_parked(&aempty[ab], ((tl >> 1) & 1) ^ 1, a.status);
+      mbar_arrive_expect_tx(&afull[ab], a_bytes);
+      for (int kb = 0; kb < KB2; ++kb) tma_load_2d(sA + ab * a_bytes + kb * a_kb, &mapA2, kb * kBK, row0, &afull[ab]);
       for (int c = cb; c < cb + NCG; ++c, ++ch) {
         const int s = ch % kDownStages;
         mbar_wait_parked(&bempty[s], ((ch / kDownStages) & 1) ^ 1, a.status);
@@ -586,7 +586,8 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.NCW);
     int tl = 0, ch = 0;
     for (int un = blockIdx.x; un < nunits; un += gridDim.x, ++tl) {
-      mbar_wait_parked(afull, tl & 1, a.status);
+      const int ab = tl & 1;
+      mbar_wait_parked(&afull[ab], (tl >> 1) & 1, a.status);
       tc_fence_after();
       for (int c = 0; c < NCG; ++c, ++ch) {
         const int s = ch % kDownStages, acc = ch & 1;
@@ -595,14 +596,14 @@ down_gemm_kernel(const __grid_constant__ CUtensorMap mapA2, const __grid_constan
         tc_fence_after();
         for (int k16 = 0; k16 < a.G / 16; ++k16) {
           const int kb = k16 >> 2, kk = k16 & 3;
-          const uint64_t ad = umma_desc_sw128(smem_u32(sA + kb * a_kb)) + 2 * kk;
+          const uint64_t ad = umma_desc_sw128(smem_u32(sA + ab * a_bytes + kb * a_kb)) + 2 * kk;
           const uint64_t bd = umma_desc_sw128(smem_u32(sB + s * b_bytes + kb * b_kb)) + 2 * kk;
           umma_bf16(tmem + acc * 256, ad, bd, idesc, k16 != 0);
         }
         umma_commit(&bempty[s]);
         umma_commit(&tfull[acc]);
       }
-      umma_commit(aempty);
+      umma_commit(&aempty[ab]);
     }
   } else if (warp < kDownEpiWarps) {  // epilogue: the tile's rows, stored in pair order as scaled fp16
     // Per 64-column slice of a row: s = 14 - exponent(max |v|) (clamped), the values scaled by
@@ -956,7 +957,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   DownArgs da{H, G, NCW, ngrp, y_sc, tile_expert, tile_row0, ntiles, pair_token, status};
   const int KB2 = (G + kBK - 1) / kBK;
   const int NCW_ = NCW;
-  const size_t d_smem = 1024 + (size_t)KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
+  const size_t d_smem = 1024 + (size_t)2 * KB2 * kTileM * 128 + (size_t)kDownStages * KB2 * NCW_ * 128 + 256 +
                         (kDownEpiWarps / 4) * 2 * 16384 + 1024;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(down_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)d_smem));
   down_gemm_kernel<<<grid, kDownThreads, d_smem, st>>>(mA2, mD, mYh, da);
