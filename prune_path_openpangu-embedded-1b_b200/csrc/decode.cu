@@ -374,7 +374,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
         l[i] = e < E ? lg[t * E + e] : -INFINITY;
       }
       if (t == 0) PPMOE_TRACE(12);
-      const uint32_t bits = select_experts_warp(l, E, a.tau_b, w, reinterpret_cast<uint32_t*>(smem + L.kbuf) + warp * 64);
+      uint32_t* kb = reinterpret_cast<uint32_t*>(smem + L.kbuf) + warp * 64;
+      const uint32_t bits = E <= 64 ? select_experts_warp<2>(l, E, a.tau_b, w, kb) : select_experts_warp(l, E, a.tau_b, w, kb);
       if (t == 0) PPMOE_TRACE(13);
 #pragma unroll
       for (int i = 0; i < kMaxExpertsPerLane; ++i) {
