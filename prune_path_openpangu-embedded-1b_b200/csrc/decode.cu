@@ -141,10 +141,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   if (tid == 0) {
     for (int s = 0; s <= a.slots; ++s) mbar_init(&bars[s], 1);
     if (NT == 1) {
-      mbar_init(bar_lg, E);
-      mbar_init(bar_red, kCluster * (HS / 4));
+      mbar_init(bar_lg, 1);  // armed below with the E logits' bytes (st.async from every rank)
+      // the cluster reduction lands by st.async, which completes bytes on this barrier: armed
+      // here with every byte of this rank's slice (8 sources x HS floats), before any peer can
+      // push (peers push only after the cluster barrier that follows)
+      mbar_init(bar_red, 1);
     }
     fence_mbar_init();
+    if (NT == 1) {
+      mbar_arrive_expect_tx(bar_lg, (uint32_t)E * 4u);
+      mbar_arrive_expect_tx(bar_red, (uint32_t)(kCluster * HS * 4));
+    }
   }
   __syncthreads();
   // every peer's barriers must be initialised before its first remote arrival: arrive here,
@@ -228,15 +235,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
     }
     __syncthreads();
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-    // thread (e, r) pushes this rank's logit of expert e into CTA r's `part` (all in parallel:
-    // each release arrival waits for its own store to land)
+    // thread (e, r) pushes this rank's logit of expert e into CTA r's `part` with st.async,
+    // which completes its 4 bytes on CTA r's bar_lg (no separate arrival)
     for (int i = tid; i < EPR * kCluster; i += kDecThreads) {
       const int e = i / kCluster, r = i % kCluster;
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) s += rpart[w * EPR + e];  // warp order
-      *cluster.map_shared_rank(part + rank * EPR + e, r) = s;
-      mbar_arrive_remote(mapa_u32(bar_lg, (uint32_t)r));
+      asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                   ::"r"(mapa_u32(part + rank * EPR + e, (uint32_t)r)), "r"(__float_as_uint(s)),
+                   "r"(mapa_u32(bar_lg, (uint32_t)r))
+                   : "memory");
     }
   } else {
     const int NTL = (EPR + 7) >> 3;  // expert tiles
@@ -845,9 +854,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       const int h4 = tid + c * kDecThreads;
       if (h4 < H / 4) {
         const int col = 4 * h4, owner = col / HS;
-        *reinterpret_cast<float4*>(cluster.map_shared_rank(recv + rank * HS + (col - owner * HS), owner)) =
-            make_float4(acc[c][0][0], acc[c][0][1], acc[c][0][2], acc[c][0][3]);
-        mbar_arrive_remote(mapa_u32(bar_red, (uint32_t)owner));
+        asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                     ::"r"(mapa_u32(recv + rank * HS + (col - owner * HS), (uint32_t)owner)),
+                     "r"(__float_as_uint(acc[c][0][0])), "r"(__float_as_uint(acc[c][0][1])),
+                     "r"(__float_as_uint(acc[c][0][2])), "r"(__float_as_uint(acc[c][0][3])),
+                     "r"(mapa_u32(bar_red, (uint32_t)owner))
+                     : "memory");
       }
     }
     mbar_wait_cluster(bar_red, 0u, a.status);
