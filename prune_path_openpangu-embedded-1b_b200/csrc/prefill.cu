@@ -527,7 +527,7 @@ struct DownArgs {
   uint32_t* status;
 };
 
-constexpr int kDownStages = 2;
+constexpr int kDownStages = 3;
 constexpr int kDownEpiWarps = 8;  // two warpgroups, each converting alternate 64-column slices
 constexpr int kDownThreads = 32 * (kDownEpiWarps + 2);
 
