@@ -34,7 +34,8 @@ import torch.distributed as dist
 from . import _lib
 from .tau_moe import TauSparseMoE, _stream_handle
 
-__all__ = ["ExpertParallelMoE", "dispatch_reference", "combine_partials", "chunk_bounds", "row_pitch"]
+__all__ = ["ExpertParallelMoE", "owned_experts", "dispatch_reference", "combine_partials", "chunk_bounds", "row_pitch",
+           "f16s_pitch", "f16s_encode", "f16s_decode"]
 
 
 def owned_experts(E: int, world: int, rank: int) -> torch.Tensor:
