@@ -136,27 +136,23 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
   // one token: the router logits and the cluster reduction are pushed into the consumer's
   // shared memory; each pushing thread arrives (release, cluster scope) on the consumer's
   // barrier after its own store
-  uint64_t* bar_lg = bars + a.slots + 1;   // E arrivals: 8 ranks x E/8 experts
-  uint64_t* bar_red = bars + a.slots + 2;  // 8 ranks x H/32 float4 units of this rank's slice
+  uint64_t* bar_lg = bars + a.slots + 1;   // the router logits of every rank (st.async bytes)
+  uint64_t* bar_red = bars + a.slots + 2;  // one token: this rank's slice of every CTA partial
   if (tid == 0) {
     for (int s = 0; s <= a.slots; ++s) mbar_init(&bars[s], 1);
-    if (NT == 1) {
-      mbar_init(bar_lg, 1);  // armed below with the E logits' bytes (st.async from every rank)
-      // the cluster reduction lands by st.async, which completes bytes on this barrier: armed
-      // here with every byte of this rank's slice (8 sources x HS floats), before any peer can
-      // push (peers push only after the cluster barrier that follows)
-      mbar_init(bar_red, 1);
-    }
+    // The router logits (and, for one token, the cluster reduction) land by st.async, which
+    // completes bytes on these barriers: each is armed here with every byte it will receive,
+    // before any peer can push (peers push only after the cluster barrier that follows).
+    mbar_init(bar_lg, 1);
+    if (NT == 1) mbar_init(bar_red, 1);
     fence_mbar_init();
-    if (NT == 1) {
-      mbar_arrive_expect_tx(bar_lg, (uint32_t)E * 4u);
-      mbar_arrive_expect_tx(bar_red, (uint32_t)(kCluster * HS * 4));
-    }
+    mbar_arrive_expect_tx(bar_lg, (uint32_t)(N * E) * 4u);
+    if (NT == 1) mbar_arrive_expect_tx(bar_red, (uint32_t)(kCluster * HS * 4));
   }
   __syncthreads();
   // every peer's barriers must be initialised before its first remote arrival: arrive here,
   // wait just before the first push (long after, so the wait is normally free)
-  if constexpr (NT == 1) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // Router operands.  Rank r owns experts [r EPR, (r+1) EPR) (EPR = E / 8): their router_eh
   // rows (H contiguous bf16 each) land in padded ring slots (pitch 2H + 16 bytes) and the
   // token rows in xs at pitch XP = H + 8, so every 8-row fragment load below is
@@ -281,13 +277,19 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       }
     }
     __syncthreads();
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // peers' barriers exist
+    // thread (t, e, r): this rank's logit of expert e for token t, summed in warp order, into
+    // CTA r's lg[t][rank EPR + e] by st.async (completing 4 bytes on CTA r's bar_lg)
     #pragma unroll 1
-    for (int i = tid; i < NT * EPR; i += kDecThreads) {
-      const int t = i / EPR, e = i - t * EPR;
+    for (int i = tid; i < N * EPR * kCluster; i += kDecThreads) {
+      const int r = i % kCluster, te = i / kCluster, t = te / EPR, e = te - t * EPR;
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) s += rpart[((size_t)w * NT + t) * (8 * NTL) + e];  // warp order
-      part[i] = s;  // [NT][EPR]
+      asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                   ::"r"(mapa_u32(lg + t * E + rank * EPR + e, (uint32_t)r)), "r"(__float_as_uint(s)),
+                   "r"(mapa_u32(bar_lg, (uint32_t)r))
+                   : "memory");
     }
   }
   PPMOE_TRACE(2);
@@ -300,14 +302,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_fused_kernel(const Deco
       lg[e] = l;
     }
   } else {
-    cluster.sync();  // every rank's expert logits visible cluster-wide
+    mbar_wait_cluster(bar_lg, 0u, a.status);  // every rank's logits pushed into lg
     PPMOE_TRACE(3);
-    // ---- full logits: expert e is owned by rank e / EPR
     #pragma unroll 1
     for (int i = tid; i < N * E; i += kDecThreads) {
-      const int t = i / E, e = i - t * E, r = e / EPR;
-      float l = bf16r(cluster.map_shared_rank(part, r)[t * EPR + (e - r * EPR)]);
-      if (a.bias) l = bf16r(l + a.bias[e]);
+      float l = bf16r(lg[i]);
+      if (a.bias) l = bf16r(l + a.bias[i % E]);
       lg[i] = l;
     }
   }
