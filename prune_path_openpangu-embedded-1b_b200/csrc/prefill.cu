@@ -169,35 +169,39 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
 }
 
 // ======================================================================== dispatch
-__global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, int* __restrict__ blockcnt) {
+__device__ __forceinline__ void count_body(int bx, const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E,
+                                           int* __restrict__ blockcnt) {
   // stage the block's 256 consecutive gate-weight rows (coalesced), then warp w counts
-  // experts w, w + 8, ... with one ballot per 32-token chunk
+  // experts w, w + (warps), ... with one ballot per 32-token chunk
   extern __shared__ __align__(16) uint8_t cn_smem[];
   const int P = E + 2;
   __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(cn_smem);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
-  for (int i = tid; i < nt * E / 2; i += 256) {  // rows wpitch elements apart (E when dense)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  const int t0 = bx * 256, nt = min(256, N - t0);
+  for (int i = tid; i < nt * E / 2; i += blockDim.x) {  // rows wpitch elements apart (E when dense)
     const int r = (2 * i) / E, c = (2 * i) % E;
     *reinterpret_cast<uint32_t*>(ws + r * P + c) =
         *reinterpret_cast<const uint32_t*>(w + (size_t)(t0 + r) * wpitch + c);
   }
   __syncthreads();
-  for (int e = warp; e < E; e += 8) {
+  for (int e = warp; e < E; e += nw) {
     int n = 0;
     for (int c = 0; c < 8; ++c) {
       const int r = c * 32 + lane;
       n += __popc(__ballot_sync(0xffffffffu, r < nt && __bfloat162float(ws[r * P + e]) > 0.f));
     }
-    if (lane == 0) blockcnt[(size_t)blockIdx.x * E + e] = n;
+    if (lane == 0) blockcnt[(size_t)bx * E + e] = n;
   }
+}
+__global__ void count_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, int* __restrict__ blockcnt) {
+  count_body(blockIdx.x, w, wpitch, N, E, blockcnt);
 }
 
 // One CTA of 1024 threads: per-expert prefix over token blocks, 128-padded expert offsets,
 // tile list, gate/up units, padding rows, activation counts.  Warp w owns experts w, w + 32,
 // ...: its lanes scan the expert's block counts 32 at a time (warp shuffles); warp 0 scans
 // the experts' tile and unit counts.
-__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E,
+__device__ __forceinline__ void scan_body(const int* __restrict__ blockcnt, int nblocks, int E,
                             int* __restrict__ blockoff, int* __restrict__ count, int* __restrict__ exp_off,
                             int* __restrict__ ntiles, int* __restrict__ tile_expert, int* __restrict__ tile_row0,
                             int* __restrict__ unit_tile, int* __restrict__ pair_token, float* __restrict__ pair_w,
@@ -266,9 +270,17 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ bloc
     for (int p = o + cnt_s[e] + lane; p < off_s[e + 1]; p += 32) { pair_token[p] = -1; pair_w[p] = 0.f; }
   }
 }
+__global__ void __launch_bounds__(1024) scan_kernel(const int* __restrict__ blockcnt, int nblocks, int E,
+                            int* __restrict__ blockoff, int* __restrict__ count, int* __restrict__ exp_off,
+                            int* __restrict__ ntiles, int* __restrict__ tile_expert, int* __restrict__ tile_row0,
+                            int* __restrict__ unit_tile, int* __restrict__ pair_token, float* __restrict__ pair_w,
+                            long long* __restrict__ act_counts) {
+  scan_body(blockcnt, nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, unit_tile, pair_token,
+            pair_w, act_counts);
+}
 
 // Per token block: (token, expert) pairs in token order within each expert.
-__global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, const int* __restrict__ blockoff,
+__device__ __forceinline__ void scatter_body(int bx, const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, const int* __restrict__ blockoff,
                                const int* __restrict__ exp_off, int* __restrict__ pair_token,
                                float* __restrict__ pair_w, int* __restrict__ tok_pairs, int* __restrict__ tok_k) {
   // The block's 256 gate-weight rows are consecutive in memory: one coalesced copy into shared
@@ -281,7 +293,7 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
   __nv_bfloat16* ws = reinterpret_cast<__nv_bfloat16*>(sc_smem);          // [256][E + 2]
   uint32_t* bm = reinterpret_cast<uint32_t*>(sc_smem + (size_t)256 * P * 2);  // [256][8]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * 256, nt = min(256, N - t0);
+  const int t0 = bx * 256, nt = min(256, N - t0);
   const int nw = blockDim.x >> 5;
   for (int i = tid; i < nt * E / 2; i += blockDim.x) {  // rows wpitch elements apart (E when dense)
     const int r = (2 * i) / E, c = (2 * i) % E;
@@ -302,7 +314,7 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
   }
   __syncthreads();
   for (int e = warp; e < E; e += nw) {
-    int run = exp_off[e] + blockoff[(size_t)blockIdx.x * E + e];
+    int run = exp_off[e] + blockoff[(size_t)bx * E + e];
     for (int c = 0; c < 8; ++c) {
       const int r = c * 32 + lane;
       const float wv = r < nt ? __bfloat162float(ws[r * P + e]) : 0.f;
@@ -318,6 +330,26 @@ __global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, 
       run += __popc(b);
     }
   }
+}
+__global__ void scatter_kernel(const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, const int* __restrict__ blockoff,
+                               const int* __restrict__ exp_off, int* __restrict__ pair_token,
+                               float* __restrict__ pair_w, int* __restrict__ tok_pairs, int* __restrict__ tok_k) {
+  scatter_body(blockIdx.x, w, wpitch, N, E, blockoff, exp_off, pair_token, pair_w, tok_pairs, tok_k);
+}
+
+// At most 256 tokens (one token block): count, scan and scatter in one CTA, one launch.
+__global__ void __launch_bounds__(1024) dispatch_one_block_kernel(
+    const __nv_bfloat16* __restrict__ w, int wpitch, int N, int E, int* __restrict__ blockcnt,
+    int* __restrict__ blockoff, int* __restrict__ count, int* __restrict__ exp_off, int* __restrict__ ntiles,
+    int* __restrict__ tile_expert, int* __restrict__ tile_row0, int* __restrict__ unit_tile,
+    int* __restrict__ pair_token, float* __restrict__ pair_w, long long* __restrict__ act_counts,
+    int* __restrict__ tok_pairs, int* __restrict__ tok_k) {
+  count_body(0, w, wpitch, N, E, blockcnt);
+  __syncthreads();  // the block's own global writes are visible to it after the barrier
+  scan_body(blockcnt, 1, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, unit_tile, pair_token, pair_w,
+            act_counts);
+  __syncthreads();
+  scatter_body(0, w, wpitch, N, E, blockoff, exp_off, pair_token, pair_w, tok_pairs, tok_k);
 }
 
 // ======================================================================== gate/up GEMM
@@ -921,11 +953,20 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   const size_t sc_smem = (size_t)256 * (E + 2) * 2;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sc_smem));
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(sc_smem + 256 * 8 * 4)));
-  count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, wpitch, N, E, blockcnt);
-  scan_kernel<<<1, 1024, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
-                                 reinterpret_cast<int*>(ws + W.unit_tile), pair_token, pair_w, reinterpret_cast<long long*>(counts));
-  scatter_kernel<<<W.nblocks, 512, sc_smem + 256 * 8 * 4, st>>>(weights, wpitch, N, E, blockoff, exp_off, pair_token, pair_w,
-                                                       reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
+  if (W.nblocks == 1) {  // one token block: count, scan and scatter in one launch
+    PPMOE_CHECK_CUDA(cudaFuncSetAttribute(dispatch_one_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)(sc_smem + 256 * 8 * 4)));
+    dispatch_one_block_kernel<<<1, 1024, sc_smem + 256 * 8 * 4, st>>>(
+        weights, wpitch, N, E, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
+        reinterpret_cast<int*>(ws + W.unit_tile), pair_token, pair_w, reinterpret_cast<long long*>(counts),
+        reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
+  } else {
+    count_kernel<<<W.nblocks, 256, sc_smem, st>>>(weights, wpitch, N, E, blockcnt);
+    scan_kernel<<<1, 1024, 0, st>>>(blockcnt, W.nblocks, E, blockoff, count, exp_off, ntiles, tile_expert, tile_row0,
+                                   reinterpret_cast<int*>(ws + W.unit_tile), pair_token, pair_w, reinterpret_cast<long long*>(counts));
+    scatter_kernel<<<W.nblocks, 512, sc_smem + 256 * 8 * 4, st>>>(weights, wpitch, N, E, blockoff, exp_off, pair_token, pair_w,
+                                                         reinterpret_cast<int*>(ws + W.tok_pairs), reinterpret_cast<int*>(ws + W.tok_k));
+  }
   PPMOE_CHECK_CUDA(cudaGetLastError());
 
   // ---- experts
