@@ -29,10 +29,14 @@ int route_compact_launch(const void*, int, int, float, int32_t*, void*, int32_t*
 
 constexpr int kTileM = 128;
 constexpr int kBK = 64;  // K elements per pipeline stage (one 128-byte swizzle row)
+// Up to this many tokens the router GEMM splits K over kRouterSplit CTAs per 128-token tile
+// (a lone CTA streaming all of K is latency-bound).
+constexpr int kRouterSplit = 8;
+constexpr int kRouterSplitMaxN = 512;
 
 struct PrefillWs {
   size_t logits, weights, blockcnt, blockoff, count, exp_off, ntiles, tile_expert, tile_row0, unit_tile, pair_token,
-      pair_w, a2, ypart, tok_pairs, tok_k, status, total;
+      pair_w, a2, ypart, tok_pairs, tok_k, rpart, status, total;
   long long max_pairs, max_tiles;
   int nblocks;
 };
@@ -46,6 +50,7 @@ static PrefillWs prefill_ws_layout(long long N, int H, int E, int G) {
   auto take = [&](size_t bytes) { size_t r = o; o = align_up(o + bytes, 1024); return r; };
   w.status = take(64);
   w.logits = take((size_t)N * E * 2);
+  w.rpart = take(N <= kRouterSplitMaxN ? (size_t)kRouterSplit * N * E * 4 : 0);
   w.weights = take((size_t)N * E * 2);
   w.blockcnt = take((size_t)w.nblocks * E * 4);
   w.blockoff = take((size_t)w.nblocks * E * 4);
@@ -73,6 +78,8 @@ struct RouterArgs {
   const float* bias;
   __nv_bfloat16* logits;
   uint32_t* status;
+  int ksplit;   // > 1: CTA (tile, blockIdx.y) covers 1/ksplit of K and writes fp32 partials
+  float* part;  // [ksplit][N][E] (ksplit > 1), summed in order by router_sum_kernel
 };
 
 
@@ -101,12 +108,13 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int tile = blockIdx.x;
+  const int tile = blockIdx.x, ks = blockIdx.y;
+  const int kb0 = KB * ks / a.ksplit, kb1 = KB * (ks + 1) / a.ksplit;  // this CTA's k-blocks
 
   if (warp == 4 && lane == 0) {  // TMA producer
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % a.stages;
-      mbar_wait_parked(&empty[s], ((kb / a.stages) & 1) ^ 1, a.status);
+    for (int kb = kb0; kb < kb1; ++kb) {
+      const int j = kb - kb0, s = j % a.stages;
+      mbar_wait_parked(&empty[s], ((j / a.stages) & 1) ^ 1, a.status);
       uint8_t* st = smem + s * stage_bytes;
       mbar_arrive_expect_tx(&full[s], stage_bytes);
       tma_load_2d(st, &mapX, kb * kBK, tile * kTileM, &full[s]);
@@ -114,14 +122,14 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
     }
   } else if (warp == 5 && lane == 0) {  // MMA issuer
     const uint32_t idesc = umma_idesc_bf16(kTileM, a.EP);
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % a.stages;
-      mbar_wait_parked(&full[s], (kb / a.stages) & 1, a.status);
+    for (int kb = kb0; kb < kb1; ++kb) {
+      const int j = kb - kb0, s = j % a.stages;
+      mbar_wait_parked(&full[s], (j / a.stages) & 1, a.status);
       tc_fence_after();
       const uint32_t sa = smem_u32(smem + s * stage_bytes);
       const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + a_bytes);
 #pragma unroll
-      for (int k = 0; k < kBK / 16; ++k) umma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+      for (int k = 0; k < kBK / 16; ++k) umma_bf16(tmem, ad + 2 * k, bd + 2 * k, idesc, (j | k) != 0);
       umma_commit(&empty[s]);
     }
     umma_commit(tfull);
@@ -132,7 +140,12 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
     for (int c0 = 0; c0 < a.EP; c0 += 32) {
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-      if (t < a.N) {
+      if (t < a.N && a.ksplit > 1) {  // fp32 partial of this K range
+        float* pr = a.part + ((size_t)ks * a.N + t) * a.E + c0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < a.E) pr[j] = v[j];
+      } else if (t < a.N) {
         if (c0 + 32 <= a.E && a.E % 8 == 0 && (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) {
           // whole 32-expert chunk: four 16-byte stores
           uint32_t pk[16];
@@ -166,6 +179,19 @@ router_gemm_kernel(const __grid_constant__ CUtensorMap mapX, const __grid_consta
     tc_fence_after();
     tmem_dealloc(tmem, ncols);
   }
+}
+
+// Logits of a K-split router GEMM: the ksplit fp32 partials summed in split order, rounded to
+// bf16 (+ optional prior, rounded again), as the one-pass epilogue does.
+__global__ void router_sum_kernel(const float* __restrict__ part, int ksplit, int N, int E, const float* __restrict__ bias,
+                                  __nv_bfloat16* __restrict__ logits) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N * E) return;
+  float v = 0.f;
+  for (int q = 0; q < ksplit; ++q) v += part[(size_t)q * N * E + i];
+  float l = bf16r(v);
+  if (bias) l = bf16r(l + bias[i % E]);
+  logits[i] = __float2bfloat16_rn(l);
 }
 
 // ======================================================================== dispatch
@@ -905,7 +931,7 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
   }
   if (mode == kPrefillRouteOnly) {  // router GEMM + selection only: the router rows alone are read
     const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;
-    RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+    RouterArgs ra{N, E, EP, H, rstages, bias, logits, status, 1, nullptr};
     const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
     PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
     router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
@@ -931,10 +957,18 @@ int prefill_launch(const void* x, int N, const void* packed, int H, int E, int G
 
   if (mode != kPrefillExperts && mode != kPrefillExpertsF16s) {
   const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;  // stages in flight, within the shared-memory budget
-  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status, 1, nullptr};
   const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
-  router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
+  if (N <= kRouterSplitMaxN && H / kBK >= kRouterSplit) {  // few tiles: split K, then sum in order
+    ra.ksplit = kRouterSplit;
+    ra.part = reinterpret_cast<float*>(ws + W.rpart);
+    router_gemm_kernel<<<dim3((N + kTileM - 1) / kTileM, kRouterSplit), 192, r_smem, st>>>(mX, mR, ra);
+    PPMOE_CHECK_CUDA(cudaGetLastError());
+    router_sum_kernel<<<(N * E + 255) / 256, 256, 0, st>>>(ra.part, kRouterSplit, N, E, bias, logits);
+  } else {
+    router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
+  }
   PPMOE_CHECK_CUDA(cudaGetLastError());
   if ((rc = route_logits_launch(logits, N, E, tau, nullptr, weights, nullptr, st))) return rc;
   }
@@ -1048,7 +1082,7 @@ int route_launch(const void* x, int N, const void* packed, int H, int E, int G, 
     if ((rc = make_map(&mR, pk + PL.router_eh, 2, d, s, b))) return rc;
   }
   const int rstages = EP <= 64 ? 8 : EP <= 128 ? 6 : 4;
-  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status};
+  RouterArgs ra{N, E, EP, H, rstages, bias, logits, status, 1, nullptr};
   const size_t r_smem = 1024 + rstages * (kTileM * 128 + (size_t)EP * 128) + 256;
   PPMOE_CHECK_CUDA(cudaFuncSetAttribute(router_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)r_smem));
   router_gemm_kernel<<<(N + kTileM - 1) / kTileM, 192, r_smem, st>>>(mX, mR, ra);
