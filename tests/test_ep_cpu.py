@@ -145,3 +145,34 @@ def test_dispatch_reference_chunks():
             assert row_of[d, toks].tolist() == list(range(pos, pos + k))
             pos += k
     assert send.shape[0] == pos
+
+
+def test_snake_assignment_partitions_and_balances():
+    """Every expert has exactly one owner; against a load falling with the expert index the
+    snake order spreads the load more evenly than a plain stride."""
+    ep = __import__(pkg().__name__ + ".ep", fromlist=["x"])
+    for E, P in [(64, 2), (64, 4), (64, 8), (16, 4), (192, 8)]:
+        owned = torch.cat([ep.owned_experts(E, P, r) for r in range(P)])
+        assert sorted(owned.tolist()) == list(range(E))
+    load = torch.exp(-1.2 * torch.log(torch.arange(1, 65, dtype=torch.float64)))  # Zipf(1.2) prior
+    for P in (2, 4, 8):
+        snake = torch.stack([load[ep.owned_experts(64, P, r)].sum() for r in range(P)])
+        stride = torch.stack([load[r::P].sum() for r in range(P)])
+        assert (snake.max() / snake.min()) < (stride.max() / stride.min())
+
+
+def test_f16s_round_trip_bound():
+    """Scaled-fp16 partial rows: every value within 2^-11 of its 64-column slice's maximum,
+    zeros and all-zero slices exact, and magnitudes far outside fp16's range survive."""
+    ep = __import__(pkg().__name__ + ".ep", fromlist=["x"])
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(37, 256, generator=g) * torch.logspace(-20, 20, 37)[:, None]
+    x[3] = 0.0
+    x[5, :64] = 0.0
+    enc = ep.f16s_encode(x)
+    assert enc.shape == (37, ep.f16s_pitch(256)) and ep.f16s_pitch(256) % 16 == 0
+    dec = ep.f16s_decode(enc, 256)
+    bound = x.abs().view(37, 4, 64).amax(-1, keepdim=True) * 2.0 ** -11
+    assert bool(((dec - x).view(37, 4, 64).abs() <= bound).all())
+    assert bool((dec[3] == 0).all()) and bool((dec[5, :64] == 0).all())
+    assert bool(torch.isfinite(dec).all())
