@@ -41,3 +41,26 @@ def test_host_validation_without_gpu():
     assert rc == -1
     with pytest.raises(L.PPMoEError):
         L.call("ppmoe_route_logits", None, 4, 64, 0.9, None, None, None)
+
+
+def test_ep_entry_points_validate_without_gpu():
+    """Expert-parallel entry points reject bad shapes, pitches and formats before any CUDA call."""
+    lib = pkg()._lib.load()
+    # scaled-fp16 partial rows: H fp16 + H / 64 exponents, padded to 16 bytes
+    assert lib.ppmoe_ep_partial_pitch(1536) == 3104 and lib.ppmoe_ep_partial_pitch(100) == 0
+    assert lib.ppmoe_ep_dispatch_workspace_bytes(4096, 4) > 0 and lib.ppmoe_ep_dispatch_workspace_bytes(10, 9) == 0
+    # more than 8 ranks, and experts not divisible by the ranks
+    rc = lib.ppmoe_ep_dispatch(16, 16, 10, 1536, 64, 9, 1, 16, 3200, 16, 16, 16, 1 << 20, None)
+    assert rc == -2 and b"ranks" in lib.ppmoe_last_error()
+    rc = lib.ppmoe_ep_dispatch(16, 16, 10, 1536, 63, 2, 1, 16, 3200, 16, 16, 16, 1 << 20, None)
+    assert rc == -2
+    # row pitch too small for H activations + E/P gate weights
+    rc = lib.ppmoe_ep_dispatch(16, 16, 10, 1536, 64, 2, 1, 16, 3072, 16, 16, 16, 1 << 20, None)
+    assert rc == -1 and b"row_pitch" in lib.ppmoe_last_error()
+    rc = lib.ppmoe_ep_experts(1024, 10, 3072, 1024, 1536, 32, 96, 0, 1024, 1024, 1 << 20, None)
+    assert rc == -1 and b"row_pitch" in lib.ppmoe_last_error()
+    rc = lib.ppmoe_ep_experts(1024, 10, 3136, 1024, 1536, 32, 96, 7, 1024, 1024, 1 << 20, None)
+    assert rc == -1 and b"partial_format" in lib.ppmoe_last_error()
+    rc = lib.ppmoe_ep_combine_f16s(16, 3000, 16, 2, 10, 1536, 16, None)
+    assert rc == -2 and b"pitch" in lib.ppmoe_last_error()
+    assert lib.ppmoe_ep_combine_f16s(16, 3104, 16, 2, 0, 1536, 16, None) == 0  # nothing to combine
