@@ -221,3 +221,16 @@ def test_decode_hidden_not_multiple_of_384(cuda):
         m = make_module(L, 0.7, cuda)
         out, lg, w = run_decode(m, x, cuda)
         check_against_oracle(L, x, 0.7, out, lg, w, what=f"H1152 N{n}")
+
+
+@pytest.mark.parametrize("scale", [0.5, 1.0])
+def test_decode_one_token_broad_selection(cuda, scale):
+    """One token selecting most experts (flat router at tau 0.95): each CTA holds more neurons
+    than the ring has slots, so the windowed path with slot refills runs."""
+    L = make_layer(17, tau=0.95, scale=scale)
+    m = make_module(L, 0.95, cuda)
+    for s in range(3):
+        x = pkg().synth.make_tokens(17 + s, 1, 1536)
+        out, lg, w = run_decode(m, x, cuda)
+        assert int((w > 0).sum()) > 30  # > 24 neurons per CTA: the windowed path
+        check_against_oracle(L, x, 0.95, out, lg, w, what=f"broad s{scale} {s}")
